@@ -1,0 +1,652 @@
+#!/usr/bin/env python
+"""Benchmark of the MLIRKernels.jl hot path on B200: HBM GB/s of the fused
+mapreduce ``sum(x.^2)`` over 2^28 Float32 (the BASELINE configuration the
+metric is quoted on), plus the other four kernels with ``--kernel``.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--kernel reduce|vadd|gather|histogram|matmul_simt|all]
+
+One process per GPU (torchrun for N > 1, NCCL).  Per-GPU work is fixed
+(weak scaling): every rank holds its own contiguous shard of the size the
+configuration names.  A step is one pass of the kernel over its shard, plus the
+single NCCL all-reduce of the partial where the path has one (reduce,
+histogram).  Rank 0 prints one JSON line per kernel.
+
+``--impl reference`` times the reference's CPU execution model (the restated
+MLIRBackend of oracle/oracle.c, all host threads) on the same configuration;
+rank 0 alone runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import operator
+import os
+import shutil
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+HBM_FALLBACK_GBS = 6650.0
+L2_BYTES = 126 * 2**20
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return HBM_FALLBACK_GBS, "fallback"
+
+
+# ----------------------------------------------------------------- clocks --
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        exe = shutil.which("nvidia-smi")
+        if exe is None:
+            return self
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        self.fh = open(self.path, "w")
+        self.proc = subprocess.Popen([exe, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                      "-i", str(self.dev), "-lms", "50"], stdout=self.fh,
+                                     stderr=subprocess.DEVNULL)
+        time.sleep(0.15)
+        return self
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------- workloads -----
+
+class Workload:
+    """One benchmark configuration on one rank."""
+
+    name = ""
+    metric = ""
+    unit = "GB/s"
+    dtype = "f32"
+
+    def __init__(self, rank: int, world: int):
+        self.rank, self.world = rank, world
+
+    # algorithmic units per step on this rank (bytes, or flops)
+    units_per_step = 0.0
+    launches_per_step = 1
+    needs_l2_flush = False
+    h2d_bytes = 0
+    d2h_bytes = 0
+
+
+def _dist_allreduce_max(x: float) -> float:
+    import torch
+    import torch.distributed as dist
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+    return x
+
+
+def make_workload(kind: str, rank: int, world: int):
+    import torch
+
+    import cutilecpu_b200 as mk
+    from cutilecpu_b200 import _lib, distributed, workloads
+
+    L = _lib.lib()
+    be = mk.MLIRCUDABackend()
+    stream = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
+
+    class Reduce(Workload):
+        name = "reduce"
+        metric = "mapreduce sum(x.^2) HBM GB/s"
+        cfg = workloads.CONFIGS["reduce"]
+
+        def __init__(self):
+            super().__init__(rank, world)
+            n = self.n = self.cfg["n"]
+            self.x_host = workloads.uniform_pm1(n, stream=1 + 100 * rank)
+            self.x = mk.MLIRArray(self.x_host)
+            self.out = torch.empty(1, dtype=torch.float64, device="cuda")
+            self.units_per_step = 4.0 * n
+            self.h2d_bytes, self.d2h_bytes = 4 * n, 8
+            self.config = {"workload": "mapreduce sum(x.^2), Float32 x ~ U[-1,1), n=2^28 per GPU "
+                                       "(configs[1]); fused single pass, fp64 accumulation",
+                           "n_per_gpu": n, "l2": "input (1 GiB) larger than L2; no flush"}
+
+        def launch(self):
+            _lib.check(L.mk_sum_sq_f32(self.out.data_ptr(), self.x.pointer(), self.n, stream()), "sum_sq")
+
+        def combine(self):
+            distributed.combine_partial(self.out, "add")
+
+        def check(self):
+            import oracle
+            got = self.out.item()
+            if world == 1:
+                want = oracle.sum_sq(self.x_host)
+                assert abs(got - want) <= 1e-5 * abs(want), (got, want)
+
+        def e2e_setup(self):
+            self.pinned = torch.from_numpy(self.x_host).pin_memory()
+            self.xd = mk.allocate(be, "Float32", self.n)
+
+        def e2e_step(self):
+            mk.copyto(be, self.xd, self.pinned)
+            res = mk.reduce.mapreduce_device(mk.abs2, operator.add, self.xd)
+            distributed.combine_partial(res, "add")
+            return res.item()
+
+        def cpu_sample(self, threads):
+            import oracle
+            Lo = oracle.lib()
+            tmp = np.empty(self.n + self.n // 512 + 2, dtype=np.float32)
+            return lambda: Lo.mlirb_sum_sq_f32(self.x_host.ctypes.data, self.n, 256, tmp.ctypes.data), \
+                self.units_per_step, "full 2^28-element sum(x.^2): materialised x.^2 + fp32 block-tree rounds"
+
+    class Vadd(Workload):
+        name = "vadd"
+        metric = "vadd HBM GB/s"
+        needs_l2_flush = True
+        cfg = workloads.CONFIGS["vadd"]
+
+        def __init__(self):
+            super().__init__(rank, world)
+            n = self.n = self.cfg["n"]
+            self.a_host = workloads.uniform01(n, stream=10 + 100 * rank)
+            self.b_host = workloads.uniform01(n, stream=11 + 100 * rank)
+            self.a, self.b = mk.MLIRArray(self.a_host), mk.MLIRArray(self.b_host)
+            self.c = mk.zeros(be, "Float32", n)
+            self.units_per_step = 12.0 * n
+            self.h2d_bytes, self.d2h_bytes = 8 * n, 4 * n
+            self.config = {"workload": "vadd c=a+b Float32 n=2^20 per GPU (configs[0])", "n_per_gpu": n,
+                           "l2": "L2 flushed (256 MiB write) before every launch"}
+
+        def launch(self):
+            _lib.check(L.mk_vadd_f32(self.c.pointer(), self.a.pointer(), self.b.pointer(), self.n, stream()),
+                       "vadd")
+
+        def combine(self):
+            pass
+
+        def check(self):
+            np.testing.assert_array_equal(mk.Array(self.c), self.a_host + self.b_host)
+
+        def e2e_setup(self):
+            self.pa = torch.from_numpy(self.a_host).pin_memory()
+            self.pb = torch.from_numpy(self.b_host).pin_memory()
+            self.pc = torch.empty(self.n, dtype=torch.float32).pin_memory()
+            self.k = mk.vadd(be, 256)
+
+        def e2e_step(self):
+            mk.copyto(be, self.a, self.pa)
+            mk.copyto(be, self.b, self.pb)
+            self.k(self.c, self.a, self.b, ndrange=self.n)
+            mk.copyto(be, self.pc, self.c)
+            torch.cuda.current_stream().synchronize()
+            return None
+
+        def cpu_sample(self, threads):
+            import oracle
+            Lo = oracle.lib()
+            c = np.empty_like(self.a_host)
+            return lambda: Lo.mlirb_vadd_f32(c.ctypes.data, self.a_host.ctypes.data, self.b_host.ctypes.data,
+                                             self.n, 256), self.units_per_step, "full n=2^20 vadd, W=256"
+
+    class Gather(Workload):
+        name = "gather"
+        metric = "indirect gather HBM GB/s (algorithmic 12 B/elem)"
+        cfg = workloads.CONFIGS["gather"]
+
+        def __init__(self):
+            super().__init__(rank, world)
+            n, na = self.n, self.na = self.cfg["n"], self.cfg["na"]
+            self.a_host = workloads.uniform01(na, stream=20)  # replicated on every rank
+            self.idx_host = workloads.indices1(n, na, stream=21 + 100 * rank)
+            self.a, self.idx = mk.MLIRArray(self.a_host), mk.MLIRArray(self.idx_host)
+            self.c = mk.zeros(be, "Float32", n)
+            self.units_per_step = 12.0 * n
+            self.h2d_bytes, self.d2h_bytes = 4 * n, 4 * n
+            self.config = {"workload": "gather c=a[idx] Float32 a 2^27 (replicated), Int32 idx 2^27 per GPU "
+                                       "uniform in [1,2^27] (configs[2])", "n_per_gpu": n,
+                           "l2": "inputs (1.5 GiB) larger than L2; no flush"}
+
+        def launch(self):
+            _lib.check(L.mk_gather_f32(self.c.pointer(), self.a.pointer(), self.na, self.idx.pointer(), self.n,
+                                       stream()), "gather")
+
+        def combine(self):
+            pass
+
+        def check(self):
+            got = mk.Array(self.c)
+            np.testing.assert_array_equal(got, self.a_host[self.idx_host.astype(np.int64) - 1])
+
+        def e2e_setup(self):
+            self.pidx = torch.from_numpy(self.idx_host).pin_memory()
+            self.pc = torch.empty(self.n, dtype=torch.float32).pin_memory()
+            self.k = mk.gather(be, 256)
+
+        def e2e_step(self):
+            mk.copyto(be, self.idx, self.pidx)
+            self.k(self.c, self.a, self.idx, ndrange=self.n)
+            mk.copyto(be, self.pc, self.c)
+            torch.cuda.current_stream().synchronize()
+
+        def cpu_sample(self, threads):
+            import oracle
+            Lo = oracle.lib()
+            c = np.empty(self.n, dtype=np.float32)
+            return lambda: Lo.mlirb_gather_f32(c.ctypes.data, self.a_host.ctypes.data, self.na,
+                                               self.idx_host.ctypes.data, self.n, 256), \
+                self.units_per_step, "full 2^27 gather, W=256"
+
+    class Histogram(Workload):
+        name = "histogram"
+        metric = "histogram HBM GB/s (4 B/key)"
+        cfg = workloads.CONFIGS["histogram"]
+        launches_per_step = 1
+
+        def __init__(self):
+            super().__init__(rank, world)
+            n, nb = self.n, self.nb = self.cfg["n"], self.cfg["nbins"]
+            self.keys_host = workloads.zipf_keys(n, nb, self.cfg["s"], stream=30 + 100 * rank)
+            self.keys = mk.MLIRArray(self.keys_host)
+            self.counts = mk.zeros(be, "UInt32", nb)
+            self.units_per_step = 4.0 * n
+            self.h2d_bytes, self.d2h_bytes = 4 * n, 4 * nb
+            self.config = {"workload": "histogram Int32 keys 2^26 per GPU ~ Zipf(1.1) on 1..4096, UInt32 counts "
+                                       "(configs[3]); counts zeroed each step", "n_per_gpu": n,
+                           "l2": "input (256 MiB) larger than L2; no flush"}
+
+        def launch(self):
+            self.counts.storage.zero_()
+            _lib.check(L.mk_hist_u32(self.counts.pointer(), self.nb, self.keys.pointer(), self.n, stream()),
+                       "hist")
+
+        def combine(self):
+            distributed.combine_counts(self.counts.storage)
+
+        def check(self):
+            if world == 1:
+                import oracle
+                np.testing.assert_array_equal(mk.Array(self.counts), oracle.hist(self.keys_host, self.nb)[0])
+
+        def e2e_setup(self):
+            self.pk = torch.from_numpy(self.keys_host).pin_memory()
+            self.pc = torch.empty(self.nb, dtype=torch.int32).pin_memory()
+            self.k = mk.histogram(be, 256)
+
+        def e2e_step(self):
+            mk.copyto(be, self.keys, self.pk)
+            self.counts.storage.zero_()
+            self.k(self.counts, self.keys, ndrange=self.n)
+            distributed.combine_counts(self.counts.storage)
+            self.pc.copy_(self.counts.storage, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+        def cpu_sample(self, threads):
+            import oracle
+            Lo = oracle.lib()
+            counts = np.zeros(self.nb, dtype=np.uint32)
+            m = (1 << 24)
+            return lambda: Lo.mlirb_hist_u32(counts.ctypes.data, self.nb, self.keys_host.ctypes.data, m, 256), \
+                4.0 * m, "first 2^24 of the 2^26 Zipf keys, per-lane atomics, W=256"
+
+    class MatmulSimt(Workload):
+        name = "matmul_simt"
+        metric = "matmul TFLOP/s (reference 16x16 SIMT algorithm)"
+        unit = "TFLOP/s"
+        cfg = workloads.CONFIGS["matmul"]
+
+        def __init__(self):
+            super().__init__(rank, world)
+            m, n, k = self.m, self.nn, self.k = self.cfg["m"], self.cfg["n"], self.cfg["k"]
+            self.A_host = workloads.normal((m, k), stream=40 + 100 * rank)
+            self.B_host = workloads.normal((k, n), stream=41)
+            self.A, self.B = mk.MLIRArray(self.A_host), mk.MLIRArray(self.B_host)
+            self.C = mk.zeros(be, "Float32", (m, n))
+            self.units_per_step = 2.0 * m * n * k
+            self.h2d_bytes, self.d2h_bytes = 4 * (m * k + k * n), 4 * m * n
+            self.config = {"workload": "mm_tiled! 16x16 SIMT, Float32 8192^3 row block per GPU (configs[4])",
+                           "m": m, "n": n, "k": k, "l2": "operands larger than L2"}
+
+        def launch(self):
+            _lib.check(L.mk_matmul_tiled16_f32(self.C.pointer(), self.A.pointer(), self.B.pointer(), self.m, self.nn,
+                                               self.k, self.m, self.k, self.m, stream()), "tiled16")
+
+        def combine(self):
+            pass
+
+        def check(self):
+            import oracle
+            ii = np.array([0, 1, 4095, 8191]); jj = np.array([0, 8191, 17, 4000])
+            got = mk.Array(self.C)[ii, jj]
+            want = oracle.matmul_entries_f64(self.A_host, self.B_host, ii, jj)
+            np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-3)
+
+        def e2e_setup(self):
+            self.pA = torch.from_numpy(self.A_host.ravel(order="F")).pin_memory()
+            self.pB = torch.from_numpy(self.B_host.ravel(order="F")).pin_memory()
+            self.pC = torch.empty(self.m * self.nn, dtype=torch.float32).pin_memory()
+            self.kern = mk.mm_tiled_simt(be, (16, 16))
+
+        def e2e_step(self):
+            mk.copyto(be, self.A, self.pA)
+            mk.copyto(be, self.B, self.pB)
+            self.kern(self.C, self.A, self.B, ndrange=(self.m, self.nn))
+            mk.copyto(be, self.pC, self.C)
+            torch.cuda.current_stream().synchronize()
+
+        def cpu_sample(self, threads):
+            import oracle
+            Lo = oracle.lib()
+            Cs = np.zeros((self.m, self.nn), dtype=np.float32, order="F")
+            cols = 64
+            return lambda: Lo.mlirb_mm_tiled16_f32(Cs.ctypes.data, self.A_host.ctypes.data, self.B_host.ctypes.data,
+                                                   self.m, self.nn, self.k, self.m, self.k, self.m, 0, cols), \
+                2.0 * self.m * cols * self.k, f"C[:, 1:{cols}] of the 8192^3 product (restated 16x16 tiles)"
+
+    table = {"reduce": Reduce, "vadd": Vadd, "gather": Gather, "histogram": Histogram,
+             "matmul_simt": MatmulSimt}
+    return table[kind]()
+
+
+# ---------------------------------------------------------------- runner ---
+
+def time_cpu(fn, budget_s: float = 10.0, max_reps: int = 20) -> tuple[float, int]:
+    fn()  # warm-up (page faults, thread pool)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < max_reps and (not times or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times), len(times)
+
+
+def run_ours(kind: str, args, rank: int, world: int, local_rank: int) -> dict | None:
+    import torch
+    import torch.distributed as dist
+
+    from cutilecpu_b200 import distributed
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    w = make_workload(kind, rank, world)
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev) if w.needs_l2_flush else None
+    s = torch.cuda.current_stream()
+
+    def step():
+        w.launch()
+        w.combine()
+
+    # correctness of the benchmarked configuration, before timing
+    step()
+    torch.cuda.synchronize()
+    w.check()
+
+    for _ in range(args.warmup):
+        if flush is not None:
+            flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    distributed.barrier(device=dev)
+
+    clocks = ClockSampler(local_rank).start() if rank == 0 else None
+    K = args.steps
+    k_start = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    k_end = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    torch.cuda.synchronize()
+    distributed.barrier(device=dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(s)
+    for i in range(K):
+        if flush is not None:
+            flush.zero_()
+        k_start[i].record(s)
+        w.launch()
+        k_end[i].record(s)
+        w.combine()
+    t1.record(s)
+    torch.cuda.synchronize()
+    distributed.barrier(device=dev)
+    clock_info = clocks.stop() if clocks is not None else None
+
+    region_ms = t0.elapsed_time(t1)
+    kern_ms = [a.elapsed_time(b) for a, b in zip(k_start, k_end)]
+    kern_avg = sum(kern_ms) / K
+    # whole-step time: the full region, or (with an L2 flush between steps)
+    # the per-step kernel + combine time without the flush writes
+    step_ms = region_ms / K if flush is None else kern_avg
+    step_ms = _dist_allreduce_max(step_ms)
+    kern_avg_max = _dist_allreduce_max(kern_avg)
+
+    # end to end through the public API with pinned host buffers
+    w.e2e_setup()
+    Ke = max(1, min(K, args.e2e_steps))
+    w.e2e_step()
+    torch.cuda.synchronize()
+    distributed.barrier(device=dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(Ke):
+        w.e2e_step()
+    e1.record(s)
+    torch.cuda.synchronize()
+    e2e_ms = _dist_allreduce_max(e0.elapsed_time(e1) / Ke)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+        fn, units, sample = w.cpu_sample(oracle.num_threads())
+        t, reps = time_cpu(fn, budget_s=args.cpu_budget)
+        cpu = {"value": round(units / t / (1e12 if w.unit == "TFLOP/s" else 1e9), 3), "unit": w.unit,
+               "cores": oracle.num_threads(), "kind": "port",
+               "sample": f"{sample}; restated MLIRBackend (oracle/oracle.c), median of {reps} reps"}
+
+    if rank != 0:
+        return None
+    scale = 1e12 if w.unit == "TFLOP/s" else 1e9
+    total_units = w.units_per_step * world
+    peak, peak_kind = peaks()
+    achieved = w.units_per_step / (kern_avg_max * 1e-3) / scale
+    roof = None
+    if w.unit == "GB/s":
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                "traffic": PROFILED_TRAFFIC.get(kind)}
+    else:
+        roof = {"bound": "simt-fp32", "achieved": round(achieved, 2), "peak": None, "unit": "TFLOP/s",
+                "frac": None, "traffic": None}
+    line = {
+        "metric": w.metric, "value": round(total_units / (step_ms * 1e-3) / scale, 2), "unit": w.unit,
+        "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": round(step_ms, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
+        "data": "synthetic (seeded numpy Philox, host-generated)",
+        "config": dict(w.config, parallelism=f"dp{world} (contiguous shards)" if world > 1 else "single GPU"),
+        "e2e": {"value": round(total_units / (e2e_ms * 1e-3) / scale, 3), "unit": w.unit,
+                "h2d_bytes_per_step": w.h2d_bytes, "d2h_bytes_per_step": w.d2h_bytes},
+        "gpu_launches": K * w.launches_per_step,
+        "roofline": roof,
+        "kernel_ms": round(kern_avg_max, 5),
+        "clocks": clock_info,
+        "cpu_baseline": cpu,
+    }
+    return line
+
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from the committed
+# ncu captures (profiles/); None until a capture exists for the kernel.
+PROFILED_TRAFFIC: dict[str, float | None] = {}
+
+
+def run_reference(kind: str, args) -> dict:
+    """The reference's CPU implementation of the path (restated MLIRBackend)."""
+    import oracle
+
+    from cutilecpu_b200 import workloads
+
+    threads = oracle.num_threads()
+    cfg = workloads.CONFIGS
+    L = oracle.lib()
+    if kind == "reduce":
+        n = cfg["reduce"]["n"]
+        x = workloads.uniform_pm1(n, stream=1)
+        tmp = np.empty(n + n // 512 + 2, dtype=np.float32)
+        fn = lambda: L.mlirb_sum_sq_f32(x.ctypes.data, n, 256, tmp.ctypes.data)  # noqa: E731
+        units, unit, metric = 4.0 * n, "GB/s", "mapreduce sum(x.^2) HBM GB/s"
+        sample = "full 2^28-element sum(x.^2) per step"
+        conf = "mapreduce sum(x.^2), Float32 x ~ U[-1,1), n=2^28 (configs[1])"
+    elif kind == "vadd":
+        n = cfg["vadd"]["n"]
+        a, b = workloads.uniform01(n, stream=10), workloads.uniform01(n, stream=11)
+        c = np.empty_like(a)
+        fn = lambda: L.mlirb_vadd_f32(c.ctypes.data, a.ctypes.data, b.ctypes.data, n, 256)  # noqa: E731
+        units, unit, metric = 12.0 * n, "GB/s", "vadd HBM GB/s"
+        sample, conf = "full n=2^20 vadd per step", "vadd c=a+b Float32 n=2^20 (configs[0])"
+    elif kind == "gather":
+        n, na = cfg["gather"]["n"], cfg["gather"]["na"]
+        a, idx = workloads.uniform01(na, stream=20), workloads.indices1(n, na, stream=21)
+        c = np.empty(n, dtype=np.float32)
+        fn = lambda: L.mlirb_gather_f32(c.ctypes.data, a.ctypes.data, na, idx.ctypes.data, n, 256)  # noqa: E731
+        units, unit, metric = 12.0 * n, "GB/s", "indirect gather HBM GB/s (algorithmic 12 B/elem)"
+        sample, conf = "full 2^27 gather per step", "gather Float32 a 2^27, Int32 idx 2^27 (configs[2])"
+    elif kind == "histogram":
+        n, nb = cfg["histogram"]["n"], cfg["histogram"]["nbins"]
+        keys = workloads.zipf_keys(n, nb, 1.1, stream=30)
+        counts = np.zeros(nb, dtype=np.uint32)
+        m = 1 << 24
+        fn = lambda: L.mlirb_hist_u32(counts.ctypes.data, nb, keys.ctypes.data, m, 256)  # noqa: E731
+        units, unit, metric = 4.0 * m, "GB/s", "histogram HBM GB/s (4 B/key)"
+        sample = "first 2^24 of the 2^26 Zipf keys per step"
+        conf = "histogram Int32 keys ~ Zipf(1.1) on 1..4096 (configs[3])"
+    else:
+        m = cfg["matmul"]["m"]
+        A = workloads.normal((m, m), stream=40)
+        B = workloads.normal((m, m), stream=41)
+        Cs = np.zeros((m, m), dtype=np.float32, order="F")
+        cols = 64
+        fn = lambda: L.mlirb_mm_tiled16_f32(Cs.ctypes.data, A.ctypes.data, B.ctypes.data, m, m, m, m, m, m,  # noqa
+                                            0, cols)
+        units, unit, metric = 2.0 * m * cols * m, "TFLOP/s", "matmul TFLOP/s (reference 16x16 SIMT algorithm)"
+        sample = f"C[:, 1:{cols}] of the 8192^3 product per step"
+        conf = "mm_tiled! Float32 8192^3 (configs[4])"
+    for _ in range(args.warmup):
+        fn()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fn()
+    dt = (time.perf_counter() - t0) / args.steps
+    scale = 1e12 if unit == "TFLOP/s" else 1e9
+    v = round(units / dt / scale, 3)
+    return {"metric": metric, "value": v, "unit": unit, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded numpy Philox, host-generated)", "impl": "reference",
+            "config": {"workload": conf, "parallelism": "host OpenMP"},
+            "cpu_baseline": {"value": v, "unit": unit, "cores": threads, "kind": "port",
+                             "sample": sample + "; restated MLIRBackend (oracle/oracle.c); the Julia reference "
+                                                "cannot run here (no julia)"},
+            "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--kernel", default="reduce",
+                    choices=["reduce", "vadd", "gather", "histogram", "matmul_simt", "all"])
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    kinds = ["reduce", "vadd", "gather", "histogram", "matmul_simt"] if args.kernel == "all" else [args.kernel]
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        if args.steps is None:
+            args.steps = 5
+        if args.warmup is None:
+            args.warmup = 1
+        for k in kinds:
+            print(json.dumps(run_reference(k, args)), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    defaults = {"reduce": (2000, 50), "vadd": (2000, 50), "gather": (200, 10), "histogram": (500, 20),
+                "matmul_simt": (3, 1)}
+    try:
+        for k in kinds:
+            a = argparse.Namespace(**vars(args))
+            a.steps = args.steps if args.steps is not None else defaults[k][0]
+            a.warmup = max(3, args.warmup if args.warmup is not None else defaults[k][1])
+            line = run_ours(k, a, rank, world, local_rank)
+            if line is not None:
+                print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,22 @@
+"""cutilecpu_b200 — B200 (sm_100a) kernels for the MLIRKernels.jl hot path.
+
+The Python side mirrors the KernelAbstractions surface the reference exposes
+(``MLIRCUDABackend``, ``MLIRArray``, ``get_backend``, ``allocate``, kernel
+launches with ``ndrange``/``workgroupsize``, AK/GPUArrays reductions); every
+computation runs in ``libkernels.so`` (C ABI: include/mk_kernels.h).
+"""
+from ._lib import KernelException, MLIRKernelsError
+from .array import (Array, MLIRArray, MLIRCUDABackend, allocate, copyto, functional, get_backend,
+                    launch_config, ones, supports_atomics, synchronize, zeros)
+from .kernels import Kernel, KernelFunction, gather, histogram, mm_tiled_simt, vadd
+from .reduce import (Broadcasted, abs2, count, identity, mapreduce, mapreducedim, maximum, minimum,
+                     positive, prod, reduce, sum)
+from . import distributed
+
+__all__ = [
+    "KernelException", "MLIRKernelsError", "Array", "MLIRArray", "MLIRCUDABackend", "allocate",
+    "copyto", "functional", "get_backend", "launch_config", "ones", "supports_atomics", "synchronize",
+    "zeros", "Kernel", "KernelFunction", "gather", "histogram", "mm_tiled_simt", "vadd", "Broadcasted",
+    "abs2", "count", "identity", "mapreduce", "mapreducedim", "maximum", "minimum", "positive", "prod",
+    "reduce", "sum", "distributed",
+]

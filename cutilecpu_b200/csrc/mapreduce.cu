@@ -1,0 +1,237 @@
+// mapreduce.cu — out = op(init, op_i f(x[i])) over an fp32 vector, in ONE
+// launch: the fused replacement for the reference's reduce path
+// (GPUArrays.mapreducedim! -> AK.mapreduce, ext/MLIRCUDAExt.jl:100-121), which
+// materialises a broadcast `x.^2` first (:103) and then runs AcceleratedKernels'
+// multi-launch block reductions with a host copy of the partials (:125-131).
+//
+// Design (HBM-bound: 4 bytes per element, read once):
+//   * persistent grid of kBlocksPerSM x SMs blocks; every thread keeps kUnroll
+//     16-byte loads in flight and accumulates in fp64 (sums/products), or exactly
+//     in fp32 (max/min).  For f in {abs2, abs, x>0} the 8 mapped values of one
+//     float4 pair are first added in fp32 (all terms >= 0: relative error of
+//     that group <= 7 ulp), then added to the fp64 accumulator; identity sums
+//     convert every term to fp64 because terms of mixed sign may cancel;
+//   * warp shuffle + shared-memory combine -> one fp64 partial per block in the
+//     per-stream scratch array;
+//   * the last block to finish (atomic ticket) folds the partials in a fixed
+//     order, applies `init`, writes out[0] and re-arms the ticket.  The result
+//     depends only on n and the grid size, so it is deterministic per device.
+// NaN handling of max/min follows Julia's `max`/`min` (a NaN operand wins) and
+// +0.0 > -0.0, which is what `maximum`/`minimum` on Float32 give.
+#include <math.h>
+#include <stdlib.h>
+
+#include "mk_common.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;  // float4 loads in flight per thread
+
+__device__ __forceinline__ float mapf(int f, float v) {
+  switch (f) {
+    case MK_F_ABS2: return __fmul_rn(v, v);
+    case MK_F_ABS: return fabsf(v);
+    case MK_F_GT0: return v > 0.0f ? 1.0f : 0.0f;
+    default: return v;
+  }
+}
+
+__device__ __forceinline__ double jl_max(double a, double b) {
+  if (a != a) return a;
+  if (b != b) return b;
+  if (a == b) return signbit(a) ? b : a;
+  return a > b ? a : b;
+}
+__device__ __forceinline__ double jl_min(double a, double b) {
+  if (a != a) return a;
+  if (b != b) return b;
+  if (a == b) return signbit(a) ? a : b;
+  return a < b ? a : b;
+}
+
+template <int OP>
+__device__ __forceinline__ double combine(double a, double b) {
+  if (OP == MK_OP_ADD) return a + b;
+  if (OP == MK_OP_MUL) return a * b;
+  if (OP == MK_OP_MAX) return jl_max(a, b);
+  return jl_min(a, b);
+}
+
+template <int OP>
+__device__ __forceinline__ double neutral() {
+  if (OP == MK_OP_ADD) return 0.0;
+  if (OP == MK_OP_MUL) return 1.0;
+  if (OP == MK_OP_MAX) return -INFINITY;
+  return INFINITY;
+}
+
+// Fold one float4 (already mapped) into the thread accumulator.
+template <int F, int OP>
+__device__ __forceinline__ void fold4(double& acc, float4 v) {
+  const float m0 = mapf(F, v.x), m1 = mapf(F, v.y), m2 = mapf(F, v.z), m3 = mapf(F, v.w);
+  if (OP == MK_OP_ADD) {
+    if (F == MK_F_IDENTITY) {
+      acc += (double)m0;
+      acc += (double)m1;
+      acc += (double)m2;
+      acc += (double)m3;
+    } else {
+      acc += (double)((m0 + m1) + (m2 + m3));
+    }
+  } else if (OP == MK_OP_MUL) {
+    acc = acc * (double)m0 * (double)m1 * (double)m2 * (double)m3;
+  } else {
+    acc = combine<OP>(acc, combine<OP>(combine<OP>((double)m0, (double)m1),
+                                       combine<OP>((double)m2, (double)m3)));
+  }
+}
+
+template <int F, int OP>
+__device__ __forceinline__ void fold1(double& acc, float v) {
+  acc = combine<OP>(acc, (double)mapf(F, v));
+}
+
+template <int OP>
+__device__ __forceinline__ double block_reduce(double v, double* smem) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = combine<OP>(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) smem[warp] = v;
+  __syncthreads();
+  v = neutral<OP>();
+  if (warp == 0) {
+    if (lane < kThreads / 32) v = smem[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = combine<OP>(v, __shfl_xor_sync(0xffffffffu, v, o));
+  }
+  return v;  // valid in thread 0
+}
+
+// x: base pointer; the first `head` (0..3) elements precede the first 16-byte
+// boundary and are folded by the first `head` threads, like the <4 tail.
+template <int F, int OP>
+__global__ void __launch_bounds__(kThreads)
+mapreduce_kernel(const float* __restrict__ x, int64_t n, int head, double init,
+                 double* __restrict__ partials, unsigned* __restrict__ ticket,
+                 double* __restrict__ out) {
+  __shared__ double smem[kThreads / 32];
+  __shared__ bool is_last;
+  const int64_t tid = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  double acc = neutral<OP>();
+
+  const float4* x4 = reinterpret_cast<const float4*>(x + head);
+  const int64_t n4 = (n - head) / 4;
+  int64_t i = tid;
+  for (; i + (kUnroll - 1) * stride < n4; i += kUnroll * stride) {
+    float4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) v[u] = __ldcs(x4 + i + u * stride);
+    if (OP == MK_OP_ADD && F != MK_F_IDENTITY) {
+      // Pair-wise fp32 grouping: 8 non-negative mapped terms per fp64 add.
+#pragma unroll
+      for (int u = 0; u < kUnroll; u += 2) {
+        float g0 = (mapf(F, v[u].x) + mapf(F, v[u].y)) + (mapf(F, v[u].z) + mapf(F, v[u].w));
+        float g1 = (mapf(F, v[u + 1].x) + mapf(F, v[u + 1].y)) +
+                   (mapf(F, v[u + 1].z) + mapf(F, v[u + 1].w));
+        acc += (double)(g0 + g1);
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) fold4<F, OP>(acc, v[u]);
+    }
+  }
+  for (; i < n4; i += stride) fold4<F, OP>(acc, __ldcs(x4 + i));
+  // Scalar head (before the first 16-byte boundary) and tail (< 4 elements).
+  const int64_t tail_start = head + n4 * 4;
+  if (tid < head) fold1<F, OP>(acc, x[tid]);
+  if (tid < n - tail_start) fold1<F, OP>(acc, x[tail_start + tid]);
+
+  double bsum = block_reduce<OP>(acc, smem);
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x] = bsum;
+    __threadfence();
+    unsigned t = atomicAdd(ticket, 1u);
+    is_last = (t == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // Last block: fold the partials in a fixed order (strided per thread, then
+  // the same shuffle tree), so the result does not depend on block timing.
+  double v = neutral<OP>();
+  for (int b = threadIdx.x; b < (int)gridDim.x; b += kThreads) v = combine<OP>(v, __ldcg(partials + b));
+  __syncthreads();  // smem reuse
+  v = block_reduce<OP>(v, smem);
+  if (threadIdx.x == 0) {
+    out[0] = combine<OP>(init, v);
+    *ticket = 0u;  // re-arm for the next reduction on this stream
+  }
+}
+
+template <int F, int OP>
+void launch(unsigned blocks, cudaStream_t s, const float* x, int64_t n, int head, double init,
+            const mk::ReduceScratch& rs, double* out) {
+  mapreduce_kernel<F, OP><<<blocks, kThreads, 0, s>>>(x, n, head, init, rs.partials, rs.ticket, out);
+}
+
+template <int F>
+int dispatch_op(int op, unsigned blocks, cudaStream_t s, const float* x, int64_t n, int head,
+                double init, const mk::ReduceScratch& rs, double* out) {
+  switch (op) {
+    case MK_OP_ADD: launch<F, MK_OP_ADD>(blocks, s, x, n, head, init, rs, out); break;
+    case MK_OP_MAX: launch<F, MK_OP_MAX>(blocks, s, x, n, head, init, rs, out); break;
+    case MK_OP_MIN: launch<F, MK_OP_MIN>(blocks, s, x, n, head, init, rs, out); break;
+    case MK_OP_MUL: launch<F, MK_OP_MUL>(blocks, s, x, n, head, init, rs, out); break;
+    default: return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: unknown op");
+  }
+  return MK_OK;
+}
+
+int blocks_per_sm() {
+  static int v = [] {
+    const char* e = getenv("MK_TUNE_REDUCE_BLOCKS_PER_SM");
+    int b = e ? atoi(e) : 8;
+    return (b >= 1 && b <= 16) ? b : 8;
+  }();
+  return v;
+}
+
+}  // namespace
+
+extern "C" int mk_mapreduce_f32(double* out_dev, const float* x, int64_t n, int f, int op,
+                                double init, void* stream) {
+  MK_ENTRY_DEVICE(dev);
+  if (n < 0) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: n must be >= 0");
+  if (!out_dev || (n > 0 && !x)) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: null pointer");
+  if (f < MK_F_IDENTITY || f > MK_F_GT0) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: unknown f");
+  if (op < MK_OP_ADD || op > MK_OP_MUL) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: unknown op");
+  cudaStream_t s = mk::as_stream(stream);
+  mk::ReduceScratch rs;
+  int rc = mk::reduce_scratch(dev, s, &rs);
+  if (rc != MK_OK) return rc;
+  int head = 0;
+  if (n > 0) {
+    head = (int)(((16u - (reinterpret_cast<uintptr_t>(x) & 15u)) & 15u) / 4u);
+    if ((reinterpret_cast<uintptr_t>(x) & 3u) != 0)
+      return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: x must be 4-byte aligned");
+    if (head > n) head = (int)n;
+  }
+  int64_t want = mk::cdiv(n, (int64_t)kThreads * kUnroll * 4);
+  int64_t cap = (int64_t)dev->sms * blocks_per_sm();
+  if (cap > mk::kMaxReduceBlocks) cap = mk::kMaxReduceBlocks;
+  unsigned blocks = (unsigned)(want < 1 ? 1 : (want > cap ? cap : want));
+  switch (f) {
+    case MK_F_IDENTITY: rc = dispatch_op<MK_F_IDENTITY>(op, blocks, s, x, n, head, init, rs, out_dev); break;
+    case MK_F_ABS2: rc = dispatch_op<MK_F_ABS2>(op, blocks, s, x, n, head, init, rs, out_dev); break;
+    case MK_F_ABS: rc = dispatch_op<MK_F_ABS>(op, blocks, s, x, n, head, init, rs, out_dev); break;
+    default: rc = dispatch_op<MK_F_GT0>(op, blocks, s, x, n, head, init, rs, out_dev); break;
+  }
+  if (rc != MK_OK) return rc;
+  return mk::check_launch("mk_mapreduce_f32: launch");
+}
+
+extern "C" int mk_sum_sq_f32(double* out_dev, const float* x, int64_t n, void* stream) {
+  return mk_mapreduce_f32(out_dev, x, n, MK_F_ABS2, MK_OP_ADD, 0.0, stream);
+}

@@ -1,0 +1,78 @@
+"""Multi-GPU partitioning: one process per GPU, ``torch.distributed`` for the
+plumbing (NCCL over NVLink on the B200 box, gloo in CPU tests).
+
+The reference is single-GPU (no ``device!``, test/test_ka_upstream.jl:6-10);
+this module is the partitioning layer the north star asks for in the launch
+path:
+
+* vadd, gather, histogram and mapreduce shard their index space into
+  contiguous ranges ``[r*n/W, (r+1)*n/W)`` (``shard_range``); vadd and gather
+  need no exchange;
+* mapreduce combines one fp64 partial per rank and histogram one u32 count
+  vector per rank with a single all-reduce (``combine_partial`` /
+  ``combine_counts``);
+* the matmul shards row blocks of A (``row_block``); B is replicated.
+
+Each function takes the process group explicitly (``None`` = the default
+group) and leaves the local computation to the caller, so the same code runs
+with NCCL device tensors and gloo host tensors.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+_REDUCE_OPS = {"add": dist.ReduceOp.SUM, "mul": dist.ReduceOp.PRODUCT,
+               "max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN}
+
+
+def world(group=None) -> tuple[int, int]:
+    """(rank, world_size) of this process, (0, 1) without a process group."""
+    if not dist.is_available() or not dist.is_initialized():
+        return 0, 1
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+def shard_range(n: int, rank: int, world_size: int) -> tuple[int, int]:
+    """Contiguous shard ``[lo, hi)`` of ``n`` elements for ``rank``; the first
+    ``n % world_size`` ranks hold one extra element."""
+    if world_size < 1 or not 0 <= rank < world_size:
+        raise ValueError(f"bad rank {rank} for world size {world_size}")
+    base, extra = divmod(n, world_size)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def row_block(m: int, rank: int, world_size: int, align: int = 128) -> tuple[int, int]:
+    """Row range of A (and C) owned by ``rank`` for the sharded matmul, in
+    multiples of ``align`` rows except for the last rank."""
+    blocks = -(-m // align)
+    lo_b, hi_b = shard_range(blocks, rank, world_size)
+    return min(lo_b * align, m), min(hi_b * align, m)
+
+
+def combine_partial(partial: torch.Tensor, op: str = "add", group=None) -> torch.Tensor:
+    """All-reduce a per-rank reduction partial in place (one fp64 scalar for
+    ``sum(x.^2)``): the single exchange step of the sharded mapreduce."""
+    if world(group)[1] > 1:
+        dist.all_reduce(partial, op=_REDUCE_OPS[op], group=group)
+    return partial
+
+
+def combine_counts(counts: torch.Tensor, group=None) -> torch.Tensor:
+    """All-reduce per-rank histogram counts in place.  u32 counts travel as
+    int32: two's-complement addition is addition mod 2^32, so the bits equal a
+    u32 sum with wrap-around."""
+    if counts.dtype not in (torch.int32, torch.int64):
+        raise TypeError(f"counts must be int32 storage, got {counts.dtype}")
+    if world(group)[1] > 1:
+        dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=group)
+    return counts
+
+
+def barrier(group=None, device: torch.device | None = None) -> None:
+    if world(group)[1] > 1:
+        if device is not None and device.type == "cuda":
+            dist.barrier(group=group, device_ids=[device.index])
+        else:
+            dist.barrier(group=group)

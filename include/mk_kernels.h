@@ -1,0 +1,122 @@
+/*
+ * mk_kernels.h — C ABI of libkernels.so, the B200 (sm_100a) kernel library
+ * that replaces the JIT-compiled GPU path of MLIRKernels.jl (gbaraldi/cuTileCPU)
+ * for five data-parallel kernels: vadd, mapreduce, gather, histogram and the
+ * 16x16 @localmem tiled matmul.
+ *
+ * Conventions (all entry points):
+ *   - Return an int status: MK_OK (0) or a negative MK_ERR_* code. On failure a
+ *     human-readable message is available from mk_last_error() (thread-local),
+ *     mirroring the descriptive Julia `error(...)` strings the reference raises
+ *     in its launcher (ext/MLIRCUDAExt.jl:428-438, 483-497, 516-537).
+ *   - Every pointer argument is a DEVICE pointer on the current CUDA device,
+ *     owned by the caller; the library never frees caller memory
+ *     (the reference launcher never allocates user data either:
+ *     ext/MLIRCUDAExt.jl:540-548).
+ *   - Every launch is asynchronous on the caller's stream (`stream` is a
+ *     cudaStream_t passed as void*; NULL = legacy default stream), as CUDA.jl
+ *     launches on its task-local stream (ext/MLIRCUDAExt.jl:546).
+ *   - Index arrays (gather indices, histogram keys) are 1-BASED Int32, as in
+ *     the Julia kernels.  Matrices are COLUMN-MAJOR (Julia layout).
+ *   - Device-side faults that the reference turns into a KernelException at the
+ *     next synchronize (src/lower.jl:1673-1703, ext/MLIRCUDAExt.jl:317-335) —
+ *     here: an out-of-range gather index or histogram key — set a per-device
+ *     error word; the offending element is skipped (gather writes 0).
+ *     mk_error_poll() synchronises the stream and returns/clears that word.
+ *   - Thread-safe: per-device state is created under a mutex; scratch used by
+ *     the reductions is private to each (device, stream) pair.
+ */
+#ifndef MK_KERNELS_H
+#define MK_KERNELS_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MK_API __attribute__((visibility("default")))
+#else
+#define MK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+#define MK_OK                 0
+#define MK_ERR_INVALID       -1  /* bad argument (size, pointer, enum)              */
+#define MK_ERR_CUDA          -2  /* a CUDA runtime/driver call failed                */
+#define MK_ERR_NCCL          -3  /* reserved for collective failures                 */
+#define MK_ERR_TIMEOUT       -4  /* a bounded device wait ran out                    */
+#define MK_ERR_DEVICE_FAULT  -5  /* a kernel flagged bad input (index out of range)  */
+
+/* ---- mapreduce selectors ------------------------------------------------ */
+/* f: the element map applied before the reduction (Julia `f` in mapreduce). */
+#define MK_F_IDENTITY 0   /* x            (sum, maximum, minimum, prod)       */
+#define MK_F_ABS2     1   /* x*x          (sum(abs2, x), sum(x.^2))           */
+#define MK_F_ABS      2   /* |x|                                              */
+#define MK_F_GT0      3   /* x > 0 ? 1 : 0  (count(>(0), x))                  */
+/* op: the associative reduction operator. */
+#define MK_OP_ADD 0
+#define MK_OP_MAX 1
+#define MK_OP_MIN 2
+#define MK_OP_MUL 3
+
+/* Library version (major*10000 + minor*100 + patch). */
+MK_API int mk_version(void);
+
+/* Message for the last failing call on this host thread ("" if none). */
+MK_API const char* mk_last_error(void);
+
+/* Set up per-device state for `device` (SM count, error word).  Optional:
+ * every entry point initialises the current device lazily.
+ * Replaces the first-launch codegen/CuModule set-up of ext/MLIRCUDAExt.jl:287-310. */
+MK_API int mk_init(int device);
+
+/* Synchronise `stream`, then return MK_ERR_DEVICE_FAULT (and clear the word)
+ * if any kernel on the current device flagged bad input since the last poll.
+ * Replaces the KernelException check of ext/MLIRCUDAExt.jl:317-335. */
+MK_API int mk_error_poll(void* stream);
+
+/* c[i] = a[i] + b[i], i in [0, n).  fp32 IEEE round-to-nearest, bit-exact.
+ * Replaces a KA launch of the vadd kernel (test/test_gpu_simt.jl:13-16,
+ * examples/reflection_and_perf.jl:11-14) through ext/MLIRCUDAExt.jl:540-548. */
+MK_API int mk_vadd_f32(float* c, const float* a, const float* b, int64_t n, void* stream);
+
+/* out_dev[0] = op(init, op_{i<n} f(x[i])) as fp64, written on the device.
+ * Sums/products accumulate in fp64 (per-thread fp32 groups of <= 8 terms);
+ * max/min are exact.  Deterministic for a given device model.  n == 0 gives init.
+ * Replaces GPUArrays.mapreducedim! -> AK.mapreduce (ext/MLIRCUDAExt.jl:100-121)
+ * and AK.reduce on an MLIRArray (test/test_downstream_ka.jl:27-31). */
+MK_API int mk_mapreduce_f32(double* out_dev, const float* x, int64_t n,
+                     int f, int op, double init, void* stream);
+
+/* sum(x.^2) == mk_mapreduce_f32(out, x, n, MK_F_ABS2, MK_OP_ADD, 0.0, stream). */
+MK_API int mk_sum_sq_f32(double* out_dev, const float* x, int64_t n, void* stream);
+
+/* c[i] = a[idx1[i] - 1], i in [0, n); idx1 is 1-based into a[0, na).
+ * Out-of-range indices write 0 and set the device error word.  Bit-exact.
+ * Replaces a KA launch of `c[i] = a[idx[i]]` (indexing semantics
+ * src/lower.jl:4031-4140, 1-based -> 0-based at :4064-4077). */
+MK_API int mk_gather_f32(float* c, const float* a, int64_t na, const int32_t* idx1,
+                  int64_t n, void* stream);
+
+/* counts[keys1[i] - 1] += 1 for i in [0, n), u32 wrap-around, ACCUMULATING into
+ * the caller's counts (as `@atomic bins[idx[i]] += 1` does).  Keys outside
+ * [1, nbins] are skipped and set the device error word.  Bit-exact.
+ * Replaces the histogram kernels of test/test_ka_cpu.jl:16-19 and
+ * test/test_gpu_simt.jl:49-73 (atomic kind: src/lower.jl:3600-3623). */
+MK_API int mk_hist_u32(uint32_t* counts, int32_t nbins, const int32_t* keys1, int64_t n,
+                void* stream);
+
+/* The reference's own algorithm on CUDA cores: one output per thread, 16x16
+ * shared-memory tiles, K % 16 ignored (examples/tiled_matmul.jl:28-48).  Kept
+ * as the SIMT comparison point for the tensor-core path; same argument rules. */
+MK_API int mk_matmul_tiled16_f32(float* C, const float* A, const float* B,
+                          int64_t M, int64_t N, int64_t K,
+                          int64_t lda, int64_t ldb, int64_t ldc, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MK_KERNELS_H */

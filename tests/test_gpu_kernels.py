@@ -1,0 +1,282 @@
+"""Parity of the CUDA kernels with the CPU oracle, called through the C ABI
+(libkernels.so via ctypes) on seeded inputs and the golden known-answer
+fixtures.  Bars: bit-exact for vadd, gather, histogram and the SIMT tiled
+matmul; rel 1e-5 (vs fp64) for the reductions."""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import golden
+from cutilecpu_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+RTOL_REDUCE = 1e-5
+
+
+@pytest.fixture(scope="module")
+def L(cuda):
+    lib = _lib.lib()
+    assert lib.mk_init(0) == 0, _lib.last_error()
+    return lib
+
+
+def dev(a: np.ndarray) -> torch.Tensor:
+    t = torch.from_numpy(np.ascontiguousarray(a).reshape(-1).view(
+        np.int32 if a.dtype == np.uint32 else a.dtype))
+    return t.to("cuda")
+
+
+def host(t: torch.Tensor, dtype=None) -> np.ndarray:
+    torch.cuda.synchronize()
+    h = t.cpu().numpy()
+    return h.view(dtype) if dtype is not None else h
+
+
+def stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def poll(L) -> int:
+    return L.mk_error_poll(stream())
+
+
+# ---------------------------------------------------------------- vadd -----
+
+@pytest.mark.parametrize("name", ["vadd_4096", "vadd_tail_1000", "vadd_tail_257"])
+def test_vadd_golden(L, name):
+    g = golden(name)
+    a, b = dev(g["a"]), dev(g["b"])
+    c = torch.zeros_like(a)
+    assert L.mk_vadd_f32(c.data_ptr(), a.data_ptr(), b.data_ptr(), a.numel(), stream()) == 0
+    np.testing.assert_array_equal(host(c), g["c"])
+
+
+@pytest.mark.parametrize("n", [1, 3, 4, 5, 255, 256, 257, 1 << 20, (1 << 22) + 3])
+@pytest.mark.parametrize("offset", [0, 1, 3])
+def test_vadd_sizes_and_misaligned_views(L, n, offset):
+    r = np.random.Generator(np.random.Philox(n * 7 + offset))
+    a_h = r.random(n + 4, dtype=np.float32); b_h = r.random(n + 4, dtype=np.float32)
+    a, b = dev(a_h), dev(b_h)
+    c = torch.full((n + 4,), -1.0, device="cuda")
+    o = offset
+    assert L.mk_vadd_f32(c.data_ptr() + 4 * o, a.data_ptr() + 4 * o, b.data_ptr() + 4 * o, n, stream()) == 0
+    got = host(c)
+    np.testing.assert_array_equal(got[o:o + n], oracle.vadd(a_h[o:o + n], b_h[o:o + n]))
+    assert (got[:o] == -1).all() and (got[o + n:] == -1).all()
+
+
+def test_vadd_empty_and_invalid(L):
+    assert L.mk_vadd_f32(0, 0, 0, 0, stream()) == 0
+    assert L.mk_vadd_f32(0, 0, 0, -1, stream()) == _lib.MK_ERR_INVALID
+    assert b"n must be" in L.mk_last_error()
+
+
+# ----------------------------------------------------------- mapreduce -----
+
+def reduce_dev(L, x: torch.Tensor, f="identity", op="add", init=0.0, n=None, off=0):
+    out = torch.empty(1, dtype=torch.float64, device="cuda")
+    rc = L.mk_mapreduce_f32(out.data_ptr(), x.data_ptr() + 4 * off, x.numel() - off if n is None else n,
+                            _lib.MK_F[f], _lib.MK_OP[op], float(init), stream())
+    assert rc == 0, _lib.last_error()
+    return host(out)[0]
+
+
+def test_reduce_sum_1_to_1024(L):
+    g = golden("reduce_1_1024")
+    assert reduce_dev(L, dev(g["x"])) == g["sum"]
+
+
+def test_reduce_gpuarrays_golden(L):
+    g = golden("gpuarrays_1024")
+    a, p, s = dev(g["a"]), dev(g["p"]), dev(g["s"])
+    assert reduce_dev(L, a) == pytest.approx(float(g["sum"]), rel=RTOL_REDUCE)
+    assert reduce_dev(L, a, op="max", init=-np.inf) == g["maximum"]
+    assert reduce_dev(L, a, op="min", init=np.inf) == g["minimum"]
+    assert reduce_dev(L, a, f="abs2") == pytest.approx(float(g["sum_abs2"]), rel=RTOL_REDUCE)
+    assert reduce_dev(L, p, op="mul", init=1.0) == pytest.approx(float(g["prod"]), rel=RTOL_REDUCE)
+    assert reduce_dev(L, s, f="gt0") == g["count_s_gt0"]
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 5, 17, 1000, 4096, 65537, (1 << 22) + 1])
+@pytest.mark.parametrize("off", [0, 1, 2, 3])
+def test_reduce_sum_sq_sizes(L, n, off):
+    r = np.random.Generator(np.random.Philox(n + 31 * off))
+    x_h = (r.random(n + off, dtype=np.float32) * 2 - 1).astype(np.float32)
+    got = reduce_dev(L, dev(x_h), f="abs2", off=off)
+    assert got == pytest.approx(oracle.sum_sq(x_h[off:]), rel=RTOL_REDUCE)
+
+
+@pytest.mark.parametrize("f,op,init", [("identity", "add", 0.0), ("abs", "add", 0.0), ("identity", "max", -np.inf),
+                                       ("identity", "min", np.inf), ("abs2", "add", 2.5), ("gt0", "add", 0.0),
+                                       ("abs", "max", -np.inf)])
+def test_reduce_ops_vs_oracle(L, f, op, init):
+    r = np.random.Generator(np.random.Philox(99))
+    x_h = (r.random(300_001, dtype=np.float32) * 2 - 1).astype(np.float32)
+    got = reduce_dev(L, dev(x_h), f, op, init)
+    want = oracle.mapreduce(x_h, f, op, init)
+    if op in ("max", "min") or f == "gt0":
+        assert got == want
+    else:
+        assert got == pytest.approx(want, rel=RTOL_REDUCE)
+
+
+def test_reduce_empty_gives_init(L):
+    out = torch.zeros(1, dtype=torch.float64, device="cuda")
+    x = torch.zeros(4, device="cuda")
+    assert L.mk_mapreduce_f32(out.data_ptr(), x.data_ptr(), 0, 0, 0, 3.5, stream()) == 0
+    assert host(out)[0] == 3.5
+
+
+def test_reduce_nan_propagates_in_max(L):
+    x = dev(np.array([1, np.nan, 2, 3, 4], dtype=np.float32))
+    assert np.isnan(reduce_dev(L, x, op="max", init=-np.inf))
+
+
+def test_reduce_deterministic_and_reusable(L):
+    r = np.random.Generator(np.random.Philox(5))
+    x = dev((r.random(1 << 24, dtype=np.float32) * 2 - 1).astype(np.float32))
+    vals = {reduce_dev(L, x, f="abs2") for _ in range(5)}
+    assert len(vals) == 1
+
+
+def test_reduce_two_streams(L):
+    """Scratch is per (device, stream): interleaved reductions on two streams agree."""
+    r = np.random.Generator(np.random.Philox(6))
+    xh = (r.random(1 << 22, dtype=np.float32)).astype(np.float32)
+    x = dev(xh)
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    outs = [torch.empty(1, dtype=torch.float64, device="cuda") for _ in range(8)]
+    torch.cuda.synchronize()
+    for i, o in enumerate(outs):
+        s = s1 if i % 2 == 0 else s2
+        assert L.mk_mapreduce_f32(o.data_ptr(), x.data_ptr(), x.numel(), 1, 0, 0.0, s.cuda_stream) == 0
+    torch.cuda.synchronize()
+    vals = [o.item() for o in outs]
+    assert len(set(vals)) == 1
+    assert vals[0] == pytest.approx(oracle.sum_sq(xh), rel=RTOL_REDUCE)
+
+
+# -------------------------------------------------------------- gather -----
+
+def gather_dev(L, a_h, idx_h, off=0):
+    a, idx = dev(a_h), dev(idx_h)
+    n = idx_h.size - off
+    c = torch.full((idx_h.size,), -7.0, device="cuda")
+    assert L.mk_gather_f32(c.data_ptr() + 4 * off, a.data_ptr(), a_h.size, idx.data_ptr() + 4 * off, n,
+                           stream()) == 0
+    return host(c)[off:]
+
+
+def test_gather_golden(L):
+    g = golden("gather_perm_4096")
+    np.testing.assert_array_equal(gather_dev(L, g["a"], g["idx"]), g["c"])
+    assert poll(L) == 0
+
+
+@pytest.mark.parametrize("n", [1, 3, 4, 7, 1000, 65536, (1 << 21) + 5])
+@pytest.mark.parametrize("off", [0, 1])
+def test_gather_random_vs_oracle(L, n, off):
+    r = np.random.Generator(np.random.Philox(n + off))
+    na = max(1, n // 2)
+    a_h = r.random(na, dtype=np.float32)
+    idx_h = r.integers(1, na + 1, size=n + off, dtype=np.int32)
+    got = gather_dev(L, a_h, idx_h, off)
+    want, rc = oracle.gather(a_h, idx_h[off:])
+    assert rc == 0
+    np.testing.assert_array_equal(got, want)
+    assert poll(L) == 0
+
+
+def test_gather_out_of_range_flags_fault(L):
+    a_h = np.arange(1, 9, dtype=np.float32)
+    idx_h = np.array([1, 0, 9, 8, -3, 2, 2, 2], dtype=np.int32)
+    got = gather_dev(L, a_h, idx_h)
+    want, rc = oracle.gather(a_h, idx_h)
+    np.testing.assert_array_equal(got, want)
+    assert rc == -5
+    assert poll(L) == _lib.MK_ERR_DEVICE_FAULT
+    assert b"gather index" in L.mk_last_error()
+    assert poll(L) == 0  # the word is cleared by the poll
+
+
+# ----------------------------------------------------------- histogram -----
+
+def hist_dev(L, keys_h, nbins, start=None, off=0):
+    keys = dev(keys_h)
+    counts = dev(np.zeros(nbins, dtype=np.uint32) if start is None else start)
+    assert L.mk_hist_u32(counts.data_ptr(), nbins, keys.data_ptr() + 4 * off, keys_h.size - off,
+                         stream()) == 0
+    return host(counts, np.uint32)
+
+
+@pytest.mark.parametrize("name", ["hist_ka_4096_256", "hist_mod_4096_8", "hist_one_65536"])
+def test_hist_golden(L, name):
+    g = golden(name)
+    np.testing.assert_array_equal(hist_dev(L, g["keys"], int(g["nbins"])), g["counts"])
+    assert poll(L) == 0
+
+
+@pytest.mark.parametrize("nbins", [1, 7, 256, 4096, 20000, 100_000])
+@pytest.mark.parametrize("off", [0, 3])
+def test_hist_random_vs_oracle(L, nbins, off):
+    r = np.random.Generator(np.random.Philox(nbins + off))
+    n = 300_007
+    keys = r.integers(1, nbins + 1, size=n, dtype=np.int32)
+    got = hist_dev(L, keys, nbins, off=off)
+    np.testing.assert_array_equal(got, oracle.hist(keys[off:], nbins)[0])
+
+
+def test_hist_zipf_vs_oracle(L):
+    from cutilecpu_b200 import workloads
+    keys = workloads.zipf_keys(1 << 22, 4096, 1.1, seed=3)
+    np.testing.assert_array_equal(hist_dev(L, keys, 4096), oracle.hist(keys, 4096)[0])
+
+
+def test_hist_accumulates_and_wraps(L):
+    start = np.zeros(16, dtype=np.uint32)
+    start[0] = 0xFFFFFFFF
+    start[5] = 10
+    keys = np.array([1, 1, 6, 16], dtype=np.int32)
+    want = oracle.hist(keys, 16, start)[0]
+    np.testing.assert_array_equal(hist_dev(L, keys, 16, start), want)
+
+
+def test_hist_bad_keys_flag_fault(L):
+    keys = np.array([0, 1, 2, 17, -1, 16] * 100, dtype=np.int32)
+    got = hist_dev(L, keys, 16)
+    np.testing.assert_array_equal(got, oracle.hist(keys, 16)[0])
+    assert poll(L) == _lib.MK_ERR_DEVICE_FAULT
+    assert b"histogram key" in L.mk_last_error()
+
+
+def test_hist_empty_and_invalid(L):
+    c = torch.zeros(4, dtype=torch.int32, device="cuda")
+    assert L.mk_hist_u32(c.data_ptr(), 4, 0, 0, stream()) == 0
+    assert L.mk_hist_u32(c.data_ptr(), 0, 0, 1, stream()) == _lib.MK_ERR_INVALID
+
+
+# -------------------------------------------------- SIMT tiled matmul -----
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (100, 70, 40), (16, 16, 15), (33, 1, 48)])
+def test_tiled16_bitexact(L, M, N, K):
+    r = np.random.Generator(np.random.Philox(M * N + K))
+    A_h = np.asfortranarray(r.standard_normal((M, K), dtype=np.float32))
+    B_h = np.asfortranarray(r.standard_normal((K, N), dtype=np.float32))
+    A, B = dev(A_h.ravel(order="F")), dev(B_h.ravel(order="F"))
+    Cd = torch.full((M * N,), -1.0, device="cuda")
+    assert L.mk_matmul_tiled16_f32(Cd.data_ptr(), A.data_ptr(), B.data_ptr(), M, N, K, M, K, M, stream()) == 0
+    got = host(Cd).reshape((M, N), order="F")
+    np.testing.assert_array_equal(got, oracle.mm_tiled16_f32(A_h, B_h))
+
+
+def test_tiled16_golden(L):
+    g = golden("mm_tiled_256")
+    A, B = dev(g["A"].ravel(order="F")), dev(g["B"].ravel(order="F"))
+    Cd = torch.empty(256 * 256, device="cuda")
+    assert L.mk_matmul_tiled16_f32(Cd.data_ptr(), A.data_ptr(), B.data_ptr(), 256, 256, 256, 256, 256, 256,
+                                   stream()) == 0
+    np.testing.assert_allclose(host(Cd).reshape((256, 256), order="F"), g["C"], rtol=1e-5)
