@@ -180,7 +180,7 @@ def make_workload(kind: str, rank: int, world: int):
 
         def e2e_step(self):
             mk.copyto(be, self.xd, self.pinned)
-            res = mk.reduce.mapreduce_device(mk.abs2, operator.add, self.xd)
+            res = mk.reductions.mapreduce_device(mk.abs2, operator.add, self.xd)
             distributed.combine_partial(res, "add")
             return res.item()
 

@@ -9,9 +9,9 @@ from ._lib import KernelException, MLIRKernelsError
 from .array import (Array, MLIRArray, MLIRCUDABackend, allocate, copyto, functional, get_backend,
                     launch_config, ones, supports_atomics, synchronize, zeros)
 from .kernels import Kernel, KernelFunction, gather, histogram, mm_tiled_simt, vadd
-from .reduce import (Broadcasted, abs2, count, identity, mapreduce, mapreducedim, maximum, minimum,
+from .reductions import (Broadcasted, abs2, count, identity, mapreduce, mapreducedim, maximum, minimum,
                      positive, prod, reduce, sum)
-from . import distributed
+from . import distributed, reductions
 
 __all__ = [
     "KernelException", "MLIRKernelsError", "Array", "MLIRArray", "MLIRCUDABackend", "allocate",

@@ -7,7 +7,7 @@ import pytest
 
 import cutilecpu_b200 as mk
 from cutilecpu_b200 import _lib, distributed
-from cutilecpu_b200.reduce import _f_name, _op_name
+from cutilecpu_b200.reductions import _f_name, _op_name
 
 
 def test_get_backend_rejects_non_mlirarray():
