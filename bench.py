@@ -134,7 +134,7 @@ def _dist_allreduce_max(x: float) -> float:
     return x
 
 
-def make_workload(kind: str, rank: int, world: int):
+def make_workload(kind: str, rank: int, world: int, n_override: int | None = None):
     import torch
 
     import cutilecpu_b200 as mk
@@ -151,7 +151,7 @@ def make_workload(kind: str, rank: int, world: int):
 
         def __init__(self):
             super().__init__(rank, world)
-            n = self.n = self.cfg["n"]
+            n = self.n = n_override or self.cfg["n"]
             self.x_host = workloads.uniform_pm1(n, stream=1 + 100 * rank)
             self.x = mk.MLIRArray(self.x_host)
             self.out = torch.empty(1, dtype=torch.float64, device="cuda")
@@ -199,7 +199,7 @@ def make_workload(kind: str, rank: int, world: int):
 
         def __init__(self):
             super().__init__(rank, world)
-            n = self.n = self.cfg["n"]
+            n = self.n = n_override or self.cfg["n"]
             self.a_host = workloads.uniform01(n, stream=10 + 100 * rank)
             self.b_host = workloads.uniform01(n, stream=11 + 100 * rank)
             self.a, self.b = mk.MLIRArray(self.a_host), mk.MLIRArray(self.b_host)
@@ -247,7 +247,7 @@ def make_workload(kind: str, rank: int, world: int):
 
         def __init__(self):
             super().__init__(rank, world)
-            n, na = self.n, self.na = self.cfg["n"], self.cfg["na"]
+            n, na = self.n, self.na = n_override or self.cfg["n"], self.cfg["na"]
             self.a_host = workloads.uniform01(na, stream=20)  # replicated on every rank
             self.idx_host = workloads.indices1(n, na, stream=21 + 100 * rank)
             self.a, self.idx = mk.MLIRArray(self.a_host), mk.MLIRArray(self.idx_host)
@@ -296,7 +296,7 @@ def make_workload(kind: str, rank: int, world: int):
 
         def __init__(self):
             super().__init__(rank, world)
-            n, nb = self.n, self.nb = self.cfg["n"], self.cfg["nbins"]
+            n, nb = self.n, self.nb = n_override or self.cfg["n"], self.cfg["nbins"]
             self.keys_host = workloads.zipf_keys(n, nb, self.cfg["s"], stream=30 + 100 * rank)
             self.keys = mk.MLIRArray(self.keys_host)
             self.counts = mk.zeros(be, "UInt32", nb)
@@ -420,7 +420,7 @@ def run_ours(kind: str, args, rank: int, world: int, local_rank: int) -> dict | 
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    w = make_workload(kind, rank, world)
+    w = make_workload(kind, rank, world, args.n)
     flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev) if w.needs_l2_flush else None
     s = torch.cuda.current_stream()
 
@@ -610,6 +610,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--n", type=int, default=None,
+                    help="override the element count of the configuration (small profiling cases)")
     args = ap.parse_args()
     kinds = ["reduce", "vadd", "gather", "histogram", "matmul_simt"] if args.kernel == "all" else [args.kernel]
 
