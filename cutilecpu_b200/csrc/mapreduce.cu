@@ -21,6 +21,9 @@
 #include <math.h>
 #include <stdlib.h>
 
+#include <mutex>
+#include <string>
+
 #include "mk_common.cuh"
 
 namespace {
@@ -234,4 +237,86 @@ extern "C" int mk_mapreduce_f32(double* out_dev, const float* x, int64_t n, int 
 
 extern "C" int mk_sum_sq_f32(double* out_dev, const float* x, int64_t n, void* stream) {
   return mk_mapreduce_f32(out_dev, x, n, MK_F_ABS2, MK_OP_ADD, 0.0, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.  Some callers cannot let a library call cudaMalloc:
+// hosts whose device memory is owned by their own pool allocator (CUDA.jl's
+// pool, torch's caching allocator) and must see every byte, or that run under
+// a fixed memory budget set at start-up.  mk_mapreduce_f32 takes its
+// per-stream scratch from cudaMalloc on first use; this entry point instead
+// uses one file-scope device array that every GPU loading the library holds
+// until exit: MK_NOALLOC_MAX_PARTIALS fp64 block partials (32 KiB) plus the
+// u32 ticket, 256-byte aligned.  The reduction kernel is the same one, with
+// the same grid, so the result is bit-identical to mk_mapreduce_f32.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocPartialBytes = sizeof(double) * MK_NOALLOC_MAX_PARTIALS;
+constexpr size_t kNoAllocBytes = kNoAllocPartialBytes + 256;  // partials, then the ticket
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_addr[64] = {};  // device address of g_noalloc_scratch, per device
+
+// Device address of the array on the current device.  Host code must not use
+// the symbol itself: on the host it names a shadow variable, not device memory.
+int noalloc_scratch(int device, unsigned char** out) {
+  if (device < 0 || device >= 64) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32_noalloc: device out of range");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return mk::fail_cuda(e, "mk_mapreduce_f32_noalloc: cudaGetSymbolAddress");
+    g_noalloc_addr[device] = static_cast<unsigned char*>(p);
+  }
+  *out = g_noalloc_addr[device];
+  return MK_OK;
+}
+
+}  // namespace
+
+extern "C" int mk_mapreduce_f32_noalloc(double* out_dev, const float* x, int64_t n, int f, int op,
+                                        double init, void* stream) {
+  MK_ENTRY_DEVICE(dev);
+  if (n < 0) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32_noalloc: n must be >= 0");
+  if (!out_dev || (n > 0 && !x)) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32_noalloc: null pointer");
+  if (f < MK_F_IDENTITY || f > MK_F_GT0) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32_noalloc: unknown f");
+  if (op < MK_OP_ADD || op > MK_OP_MUL) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32_noalloc: unknown op");
+  if (n > 0 && (reinterpret_cast<uintptr_t>(x) & 3u) != 0)
+    return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32_noalloc: x must be 4-byte aligned");
+  int64_t want = mk::cdiv(n, (int64_t)kThreads * kUnroll * 4);
+  int64_t cap = (int64_t)dev->sms * blocks_per_sm();
+  if (cap > mk::kMaxReduceBlocks) cap = mk::kMaxReduceBlocks;
+  const int64_t blocks = want < 1 ? 1 : (want > cap ? cap : want);
+  // One partial slot per block: the grid may not outgrow the static array.
+  if (blocks > MK_NOALLOC_MAX_PARTIALS)
+    return mk::fail(MK_ERR_INVALID,
+                    "mk_mapreduce_f32_noalloc: the launch needs " + std::to_string(blocks) +
+                        " block partials; the static scratch holds " + std::to_string(MK_NOALLOC_MAX_PARTIALS));
+  unsigned char* base = nullptr;
+  int rc = noalloc_scratch(dev->id, &base);
+  if (rc != MK_OK) return rc;
+  cudaStream_t s = mk::as_stream(stream);
+  mk::ReduceScratch rs;
+  rs.partials = reinterpret_cast<double*>(base);
+  rs.ticket = reinterpret_cast<unsigned*>(base + kNoAllocPartialBytes);
+  // The array keeps whatever the previous call left: the ticket must start at 0.
+  cudaError_t e = cudaMemsetAsync(rs.ticket, 0, sizeof(unsigned), s);
+  if (e != cudaSuccess) return mk::fail_cuda(e, "mk_mapreduce_f32_noalloc: clearing the ticket");
+  int head = 0;
+  if (n > 0) {
+    head = (int)(((16u - (reinterpret_cast<uintptr_t>(x) & 15u)) & 15u) / 4u);
+    if (head > n) head = (int)n;
+  }
+  const unsigned ub = (unsigned)blocks;
+  switch (f) {
+    case MK_F_IDENTITY: rc = dispatch_op<MK_F_IDENTITY>(op, ub, s, x, n, head, init, rs, out_dev); break;
+    case MK_F_ABS2: rc = dispatch_op<MK_F_ABS2>(op, ub, s, x, n, head, init, rs, out_dev); break;
+    case MK_F_ABS: rc = dispatch_op<MK_F_ABS>(op, ub, s, x, n, head, init, rs, out_dev); break;
+    default: rc = dispatch_op<MK_F_GT0>(op, ub, s, x, n, head, init, rs, out_dev); break;
+  }
+  if (rc != MK_OK) return rc;
+  return mk::check_launch("mk_mapreduce_f32_noalloc: launch");
 }

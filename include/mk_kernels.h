@@ -90,6 +90,24 @@ MK_API int mk_vadd_f32(float* c, const float* a, const float* b, int64_t n, void
 MK_API int mk_mapreduce_f32(double* out_dev, const float* x, int64_t n,
                      int f, int op, double init, void* stream);
 
+/* Allocation-free mk_mapreduce_f32, for callers that cannot let a library
+ * call cudaMalloc (device memory owned by the host's own pool allocator, e.g.
+ * CUDA.jl's or torch's, or a fixed budget set at start-up).  It has no
+ * counterpart in the reference.  Its scratch is one static device array that
+ * every GPU loading libkernels.so holds until exit: MK_NOALLOC_MAX_PARTIALS
+ * fp64 block partials (32 KiB) and a ticket word.  It calls no cudaMalloc,
+ * cudaFree or allocating library routine.  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress); make that first call
+ * before any stream capture.  All calls on a device share the array, so calls
+ * that overlap on the GPU (e.g. on two streams at once) race; serialise them.
+ * Each call clears the ticket before its launch.  A launch that would need more
+ * block partials than the array holds is rejected with MK_ERR_INVALID; n itself
+ * is not limited because the grid strides over x.  Same result, bit for bit,
+ * as mk_mapreduce_f32. */
+#define MK_NOALLOC_MAX_PARTIALS 4096
+MK_API int mk_mapreduce_f32_noalloc(double* out_dev, const float* x, int64_t n,
+                                    int f, int op, double init, void* stream);
+
 /* sum(x.^2) == mk_mapreduce_f32(out, x, n, MK_F_ABS2, MK_OP_ADD, 0.0, stream). */
 MK_API int mk_sum_sq_f32(double* out_dev, const float* x, int64_t n, void* stream);
 
