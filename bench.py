@@ -50,6 +50,19 @@ def peaks() -> tuple[float, str]:
     return HBM_FALLBACK_GBS, "fallback"
 
 
+def tensor_peak() -> tuple[float, str]:
+    """3xTF32 roofline: dense TF32 runs at half the bf16 rate and every fp32
+    product costs three TF32 products, so peak = bf16 / 2 / 3."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    bf16, kind = 1590.0, "fallback"
+    if p.exists():
+        try:
+            bf16, kind = float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except Exception:
+            pass
+    return round(bf16 / 6.0, 2), f"{kind} bf16 burst / 2 (tf32) / 3 (3xTF32)"
+
+
 # ----------------------------------------------------------------- clocks --
 
 class ClockSampler:
@@ -207,7 +220,7 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             self.units_per_step = 12.0 * n
             self.h2d_bytes, self.d2h_bytes = 8 * n, 4 * n
             self.config = {"workload": "vadd c=a+b Float32 n=2^20 per GPU (configs[0])", "n_per_gpu": n,
-                           "l2": "L2 flushed (256 MiB write) before every launch"}
+                           "l2": "L2 flushed (256 MiB read) before every launch"}
 
         def launch(self):
             _lib.check(L.mk_vadd_f32(self.c.pointer(), self.a.pointer(), self.b.pointer(), self.n, stream()),
@@ -394,8 +407,62 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
                                                    self.m, self.nn, self.k, self.m, self.k, self.m, 0, cols), \
                 2.0 * self.m * cols * self.k, f"C[:, 1:{cols}] of the 8192^3 product (restated 16x16 tiles)"
 
+    class Matmul(Workload):
+        name = "matmul"
+        metric = "matmul TFLOP/s (3xTF32 on tcgen05 tensor cores)"
+        unit = "TFLOP/s"
+        cfg = workloads.CONFIGS["matmul"]
+
+        def __init__(self):
+            super().__init__(rank, world)
+            m, n, k = self.m, self.nn, self.k = self.cfg["m"], self.cfg["n"], self.cfg["k"]
+            self.A_host = workloads.normal((m, k), stream=40 + 100 * rank)
+            self.B_host = workloads.normal((k, n), stream=41)
+            self.A, self.B = mk.MLIRArray(self.A_host), mk.MLIRArray(self.B_host)
+            self.C = mk.zeros(be, "Float32", (m, n))
+            self.units_per_step = 2.0 * m * n * k
+            self.h2d_bytes, self.d2h_bytes = 4 * (m * k + k * n), 4 * m * n
+            self.config = {"workload": "mm_tiled! C=A*B Float32 8192^3 per GPU (configs[4]); tcgen05 3xTF32, split pre-pass included",
+                           "m": m, "n": n, "k": k, "l2": "operands larger than L2"}
+
+        def launch(self):
+            _lib.check(L.mk_sgemm_3xtf32(self.C.pointer(), self.A.pointer(), self.B.pointer(), self.m, self.nn,
+                                               self.k, self.m, self.k, self.m, stream()), "sgemm")
+
+        def combine(self):
+            pass
+
+        def check(self):
+            import oracle
+            ii = np.array([0, 1, 4095, 8191]); jj = np.array([0, 8191, 17, 4000])
+            got = mk.Array(self.C)[ii, jj]
+            want = oracle.matmul_entries_f64(self.A_host, self.B_host, ii, jj)
+            np.testing.assert_allclose(got, want, rtol=1e-4, atol=2e-4)
+
+        def e2e_setup(self):
+            self.pA = torch.from_numpy(self.A_host.ravel(order="F")).pin_memory()
+            self.pB = torch.from_numpy(self.B_host.ravel(order="F")).pin_memory()
+            self.pC = torch.empty(self.m * self.nn, dtype=torch.float32).pin_memory()
+            self.kern = mk.mm_tiled(be, (16, 16))
+
+        def e2e_step(self):
+            mk.copyto(be, self.A, self.pA)
+            mk.copyto(be, self.B, self.pB)
+            self.kern(self.C, self.A, self.B, ndrange=(self.m, self.nn))
+            mk.copyto(be, self.pC, self.C)
+            torch.cuda.current_stream().synchronize()
+
+        def cpu_sample(self, threads):
+            import oracle
+            Lo = oracle.lib()
+            Cs = np.zeros((self.m, self.nn), dtype=np.float32, order="F")
+            cols = 64
+            return lambda: Lo.mlirb_mm_tiled16_f32(Cs.ctypes.data, self.A_host.ctypes.data, self.B_host.ctypes.data,
+                                                   self.m, self.nn, self.k, self.m, self.k, self.m, 0, cols), \
+                2.0 * self.m * cols * self.k, f"C[:, 1:{cols}] of the 8192^3 product (restated 16x16 tiles)"
+
     table = {"reduce": Reduce, "vadd": Vadd, "gather": Gather, "histogram": Histogram,
-             "matmul_simt": MatmulSimt}
+             "matmul": Matmul, "matmul_simt": MatmulSimt}
     return table[kind]()
 
 
@@ -421,7 +488,9 @@ def run_ours(kind: str, args, rank: int, world: int, local_rank: int) -> dict | 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     w = make_workload(kind, rank, world, args.n)
-    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev) if w.needs_l2_flush else None
+    # L2 flush between launches: READ a 256 MiB buffer (2x L2), so the lines
+    # it leaves behind are clean and the next launch pays no write-backs
+    flush = torch.ones(256 * 2**20 // 4, dtype=torch.float32, device=dev) if w.needs_l2_flush else None
     s = torch.cuda.current_stream()
 
     def step():
@@ -435,7 +504,7 @@ def run_ours(kind: str, args, rank: int, world: int, local_rank: int) -> dict | 
 
     for _ in range(args.warmup):
         if flush is not None:
-            flush.zero_()
+            flush_out = flush.sum()  # noqa: F841
         step()
     torch.cuda.synchronize()
     distributed.barrier(device=dev)
@@ -451,7 +520,7 @@ def run_ours(kind: str, args, rank: int, world: int, local_rank: int) -> dict | 
     t0.record(s)
     for i in range(K):
         if flush is not None:
-            flush.zero_()
+            flush_out = flush.sum()  # noqa: F841
         k_start[i].record(s)
         w.launch()
         k_end[i].record(s)
@@ -505,6 +574,10 @@ def run_ours(kind: str, args, rank: int, world: int, local_rank: int) -> dict | 
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                 "traffic": PROFILED_TRAFFIC.get(kind)}
+    elif kind == "matmul":
+        tp, tk = tensor_peak()
+        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tp, "unit": "TFLOP/s",
+                "frac": round(achieved / tp, 4), "peak_source": tk, "traffic": PROFILED_TRAFFIC.get(kind)}
     else:
         roof = {"bound": "simt-fp32", "achieved": round(achieved, 2), "peak": None, "unit": "TFLOP/s",
                 "frac": None, "traffic": None}
@@ -606,14 +679,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--kernel", default="reduce",
-                    choices=["reduce", "vadd", "gather", "histogram", "matmul_simt", "all"])
+                    choices=["reduce", "vadd", "gather", "histogram", "matmul", "matmul_simt", "all"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--n", type=int, default=None,
                     help="override the element count of the configuration (small profiling cases)")
     args = ap.parse_args()
-    kinds = ["reduce", "vadd", "gather", "histogram", "matmul_simt"] if args.kernel == "all" else [args.kernel]
+    kinds = ["reduce", "vadd", "gather", "histogram", "matmul", "matmul_simt"] if args.kernel == "all" else [args.kernel]
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -636,7 +709,7 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     defaults = {"reduce": (2000, 50), "vadd": (2000, 50), "gather": (200, 10), "histogram": (500, 20),
-                "matmul_simt": (3, 1)}
+                "matmul": (20, 3), "matmul_simt": (3, 1)}
     try:
         for k in kinds:
             a = argparse.Namespace(**vars(args))

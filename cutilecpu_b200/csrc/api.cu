@@ -5,6 +5,8 @@
 // 287-310 compiles and caches a CuFunction; :317-335 wires CUDA.jl's exception
 // flag).  Here the kernels are precompiled for sm_100a, so "initialisation" is
 // only: query the SM count, locate the error word, and hand out scratch.
+#include <stdlib.h>
+
 #include <map>
 #include <mutex>
 #include <utility>
@@ -22,6 +24,11 @@ static std::mutex g_mu;
 static constexpr int kMaxDevices = 64;
 static Device g_devices[kMaxDevices];
 static std::map<std::pair<int, cudaStream_t>, ReduceScratch> g_scratch;
+struct Workspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+static std::map<std::pair<int, cudaStream_t>, Workspace> g_workspace;
 
 int fail(int code, const std::string& msg) {
   t_last_error = msg;
@@ -103,6 +110,38 @@ int reduce_scratch(Device* d, cudaStream_t s, ReduceScratch* out) {
   g_scratch[key] = rs;
   *out = rs;
   return MK_OK;
+}
+
+int stream_workspace(Device* d, cudaStream_t s, size_t bytes, void** out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Workspace& w = g_workspace[std::make_pair(d->id, s)];
+  if (w.bytes < bytes) {
+    if (w.ptr) {
+      // the old buffer may still be read by work queued on this stream
+      cudaError_t e = cudaStreamSynchronize(s);
+      if (e != cudaSuccess) return fail_cuda(e, "workspace: cudaStreamSynchronize");
+      cudaFree(w.ptr);
+      w.ptr = nullptr;
+      w.bytes = 0;
+    }
+    cudaError_t e = cudaMalloc(&w.ptr, bytes);
+    if (e != cudaSuccess) {
+      w.ptr = nullptr;
+      return fail_cuda(e, "workspace: cudaMalloc");
+    }
+    w.bytes = bytes;
+  }
+  *out = w.ptr;
+  return MK_OK;
+}
+
+unsigned long long wait_limit_cycles() {
+  static unsigned long long v = [] {
+    const char* e = getenv("MK_WAIT_LIMIT_CYCLES");
+    unsigned long long x = e ? strtoull(e, nullptr, 10) : 0ull;
+    return x ? x : (1ull << 32);
+  }();
+  return v;
 }
 
 }  // namespace mk

@@ -24,7 +24,7 @@ constexpr int kThreads = 1024;
 struct Tune {
   int blocks_per_sm = 2;
   int replicas = 2;
-  int aggregate = 1;
+  int aggregate = 0;
 };
 
 const Tune& tune() {
@@ -70,8 +70,27 @@ hist_smem(unsigned* __restrict__ counts, uint32_t nbins, const int32_t* __restri
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   const int4* k4 = reinterpret_cast<const int4*>(keys + head);
   const int64_t n4 = (n - head) / 4;
-  // Uniform trip count per warp keeps match.any's participants whole.
-  for (int64_t base = (int64_t)blockIdx.x * kThreads; base < n4; base += stride) {
+  // Two int4 key vectors in flight per thread; uniform trip count per warp
+  // keeps match.any's participants whole in the aggregating form.
+  int64_t base = (int64_t)blockIdx.x * kThreads;
+  for (; base + stride < n4; base += 2 * stride) {
+    const int64_t i = base + threadIdx.x;
+    const bool second = i + stride < n4;
+    const int4 k0 = __ldcs(k4 + i);
+    int4 k1 = make_int4(1, 1, 1, 1);
+    if (second) k1 = __ldcs(k4 + i + stride);
+    add_key<AGG>(rep, nbins, k0.x, bad);
+    add_key<AGG>(rep, nbins, k0.y, bad);
+    add_key<AGG>(rep, nbins, k0.z, bad);
+    add_key<AGG>(rep, nbins, k0.w, bad);
+    if (second) {
+      add_key<AGG>(rep, nbins, k1.x, bad);
+      add_key<AGG>(rep, nbins, k1.y, bad);
+      add_key<AGG>(rep, nbins, k1.z, bad);
+      add_key<AGG>(rep, nbins, k1.w, bad);
+    }
+  }
+  for (; base < n4; base += stride) {
     const int64_t i = base + threadIdx.x;
     if (i < n4) {
       const int4 k = __ldcs(k4 + i);

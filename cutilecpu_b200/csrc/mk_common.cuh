@@ -43,6 +43,15 @@ struct ReduceScratch {
 };
 int reduce_scratch(Device* d, cudaStream_t s, ReduceScratch* out);
 
+// Growable device workspace private to one (device, stream) pair, for kernels
+// that stage re-laid-out operands (the 3xTF32 GEMM's hi/lo panels).  Grows with
+// cudaMalloc (after a cudaFree of the smaller buffer); never shrinks.
+int stream_workspace(Device* d, cudaStream_t s, size_t bytes, void** out);
+
+// Bounded device waits give up after this many SM clock cycles (env
+// MK_WAIT_LIMIT_CYCLES overrides; default ~2 s at 1.9 GHz).
+unsigned long long wait_limit_cycles();
+
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }

@@ -1,0 +1,456 @@
+// sgemm_tf32x3.cu — C = A*B in fp32 on the 5th-generation tensor cores
+// (tcgen05, TMEM accumulators, TMA), with 3xTF32 split precision.
+//
+// Replaces the reference's 16x16 @localmem SIMT kernel mm_tiled!
+// (examples/tiled_matmul.jl:28-48): same operands (column-major, Julia
+// layout) and the same K rule (only 16*floor(K/16) terms, :34), computed as
+//     C = Ahi*Bhi + Ahi*Blo + Alo*Bhi            (Alo*Blo dropped)
+// with x = hi + lo, hi = rna_tf32(x), lo = rna_tf32(x - hi): every operand
+// the tensor core sees is an exact TF32 value, products are exact and the
+// accumulation is fp32 in TMEM, so the result is within ~1e-6 relative of an
+// fp64 GEMM (the split method of Ootomo & Yokota, 2022).
+//
+// Two launches per call:
+//  1. split: A and B are re-laid out K-major into a per-stream workspace with
+//     each 16-wide k-block stored as [hi(16) | lo(16)], i.e. one 128-byte row
+//     segment per (row, k-block).  A is transposed on the way (column-major A
+//     is M-major); B is already K-major.
+//  2. gemm: one CTA per 128x256 tile of C, 10 warps:
+//       warp 0     TMA producer: per k-block one 128x32 box of A2 and one
+//                  256x32 box of B2 (128B swizzle) into a 4-stage ring;
+//       warp 1     MMA issuer: per stage 6 x tcgen05.mma.kind::tf32 (M=128,
+//                  N=256, K=8): hi.hi, hi.lo, lo.hi over the two k-halves,
+//                  addressed by offsetting the descriptor start inside the
+//                  swizzle atom; tcgen05.commit frees the stage;
+//       warps 2-9  epilogue: the tensor core accumulates each chunk of 128 k
+//                  (8 k-blocks) afresh into one of two 256-column TMEM buffers;
+//                  the epilogue warps (each a 32-lane quarter x 128 columns)
+//                  drain a finished chunk with tcgen05.ld 32x32b and add it into
+//                  fp32 registers with round-to-nearest, while the MMAs of the
+//                  next chunk run into the other buffer.  The tensor core's
+//                  internal fp32 accumulation is biased (it does not round to
+//                  nearest); bounding it to 128 terms keeps the K=8192 result
+//                  within 1e-5 of fp64.  Finally coalesced column-major stores.
+// Every mbarrier wait is bounded (mk::wait_limit_cycles); a timeout raises
+// ERRBIT_TIMEOUT in the device error word, stops the other roles, drains the
+// producer's in-flight copies (bounded), frees TMEM and returns.
+// No TMA multicast is used anywhere.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "mk_common.cuh"
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int KB = 16;                       // k per block (per split pair)
+constexpr int ROWF = 2 * KB;                 // floats per row segment: hi(16) | lo(16)
+constexpr int STAGES = 4;
+constexpr int A_STAGE = BM * ROWF * 4;       // 16 KiB
+constexpr int B_STAGE = BN * ROWF * 4;       // 32 KiB
+constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+constexpr int EPI_WARPS = 8;
+constexpr int kThreads = 32 * (2 + EPI_WARPS);  // producer, MMA, 8 epilogue warps
+constexpr int CHUNK_KB = 8;                      // k-blocks per TMEM accumulation chunk (128 k)
+constexpr uint32_t TMEM_COLS = 2 * BN;           // two 256-column accumulators
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+
+// kind::tf32 instruction descriptor: D f32, A/B tf32, both K-major, M=128, N=256.
+constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                           ((uint32_t)(BM >> 4) << 24);
+
+// ---------------------------------------------------------------- PTX ------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete; false on timeout or when
+// another role raised the abort flag.
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, unsigned long long limit,
+                                             volatile int* abort_flag) {
+  const long long t0 = clock64();
+  uint32_t spins = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++spins & 63u) == 0) {
+      if (*abort_flag) return false;
+      if ((unsigned long long)(clock64() - t0) > limit) return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128B swizzle, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i gets lane (base lane + i).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t u;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x));
+  return __uint_as_float(u);
+}
+
+// ------------------------------------------------------------- split -------
+
+// A (M x K column-major, lda) -> A2 (M rows x 2Kt, row-major): one block per
+// 64 rows x one 16-wide k-block, transposed through shared memory.
+__global__ void __launch_bounds__(256) split_a(float* __restrict__ A2, const float* __restrict__ A, int64_t M,
+                                               int64_t lda, int nkb) {
+  __shared__ float t[KB][65];
+  const int64_t m0 = (int64_t)blockIdx.x * 64;
+  const int kb = blockIdx.y;
+  for (int e = threadIdx.x; e < KB * 64; e += 256) {
+    const int kk = e >> 6, mm = e & 63;
+    const int64_t m = m0 + mm;
+    t[kk][mm] = (m < M) ? A[m + (int64_t)(kb * KB + kk) * lda] : 0.0f;
+  }
+  __syncthreads();
+  const int64_t row_len = (int64_t)nkb * ROWF;
+  for (int e = threadIdx.x; e < 64 * ROWF; e += 256) {
+    const int mm = e >> 5, j = e & 31;
+    const int64_t m = m0 + mm;
+    if (m < M) {
+      const float x = t[j & 15][mm];
+      const float hi = tf32_rna(x);
+      A2[m * row_len + (int64_t)kb * ROWF + j] = (j < KB) ? hi : tf32_rna(x - hi);
+    }
+  }
+}
+
+// B (K x N column-major, ldb) -> B2 (N rows x 2Kt): already K-major; B2 is
+// written linearly.
+__global__ void __launch_bounds__(256) split_b(float* __restrict__ B2, const float* __restrict__ B, int64_t N,
+                                               int64_t ldb, int nkb) {
+  const int64_t total = N * (int64_t)nkb * ROWF;
+  const int64_t stride = (int64_t)gridDim.x * 256;
+  for (int64_t e = (int64_t)blockIdx.x * 256 + threadIdx.x; e < total; e += stride) {
+    const int j = (int)(e & 31);
+    const int64_t t = e >> 5;
+    const int kb = (int)(t % nkb);
+    const int64_t n = t / nkb;
+    const float x = B[(int64_t)kb * KB + (j & 15) + n * ldb];
+    const float hi = tf32_rna(x);
+    B2[e] = (j < KB) ? hi : tf32_rna(x - hi);
+  }
+}
+
+// -------------------------------------------------------------- gemm -------
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+sgemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+             float* __restrict__ C, int64_t M, int64_t N, int64_t ldc, int nkb, unsigned long long limit,
+             unsigned* __restrict__ err) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  // bars: [0,S) full, [S,2S) empty, 2S+{0,1} acc_full, 2S+{2,3} acc_empty, 2S+4 done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m0 = (int64_t)blockIdx.y * BM;
+  const int64_t n0 = (int64_t)blockIdx.x * BN;
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
+  const uint32_t accf0 = smem_u32(bars + 2 * STAGES), acce0 = smem_u32(bars + 2 * STAGES + 2);
+  const uint32_t done = smem_u32(bars + 2 * STAGES + 4);
+  const int nchunks = (nkb + CHUNK_KB - 1) / CHUNK_KB;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf0 + 8 * b, 1);
+      mbar_init(acce0 + 8 * b, EPI_WARPS);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer
+      const uint32_t smem0 = smem_u32(smem);
+      int issued = 0;
+      bool ok = true;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES;
+        if (kb >= STAGES && !wait_bounded(empty0 + 8 * s, ((kb / STAGES) - 1) & 1, limit, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(full0 + 8 * s, STAGE_BYTES);
+        const uint32_t dst = smem0 + s * STAGE_BYTES;
+        tma_load_2d(dst, &tmA, kb * ROWF, (int)m0, full0 + 8 * s);
+        tma_load_2d(dst + A_STAGE, &tmB, kb * ROWF, (int)n0, full0 + 8 * s);
+        ++issued;
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(err, mk::ERRBIT_TIMEOUT);
+        // drain: the last (up to STAGES) copies may still be landing in smem
+        volatile int no_abort = 0;
+        for (int kb = issued - 1; kb >= 0 && kb >= issued - STAGES; --kb)
+          wait_bounded(full0 + 8 * (kb % STAGES), (kb / STAGES) & 1, limit, &no_abort);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer: chunk c accumulates afresh into TMEM buffer c & 1
+      const uint32_t smem0 = smem_u32(smem);
+      bool ok = true;
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int b = c & 1;
+        if (c >= 2 && !wait_bounded(acce0 + 8 * b, ((c >> 1) - 1) & 1, limit, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(b * BN);
+        const int kb_end = min(nkb, (c + 1) * CHUNK_KB);
+        for (int kb = c * CHUNK_KB; kb < kb_end; ++kb) {
+          const int s = kb % STAGES;
+          if (!wait_bounded(full0 + 8 * s, (kb / STAGES) & 1, limit, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem0 + s * STAGE_BYTES, bb = a + A_STAGE;
+          // (A offset, B offset) in bytes inside the 128-byte row: k-halves
+          // at +0/+32 (hi) and +64/+96 (lo).
+          mma_tf32(d, smem_desc(a + 0), smem_desc(bb + 0), kb > c * CHUNK_KB ? 1u : 0u);
+          mma_tf32(d, smem_desc(a + 32), smem_desc(bb + 32), 1u);
+          mma_tf32(d, smem_desc(a + 0), smem_desc(bb + 64), 1u);
+          mma_tf32(d, smem_desc(a + 32), smem_desc(bb + 96), 1u);
+          mma_tf32(d, smem_desc(a + 64), smem_desc(bb + 0), 1u);
+          mma_tf32(d, smem_desc(a + 96), smem_desc(bb + 32), 1u);
+          mma_commit(empty0 + 8 * s);
+        }
+        if (ok) mma_commit(accf0 + 8 * b);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(err, mk::ERRBIT_TIMEOUT);
+      }
+      // "done" completes once every MMA issued so far has finished
+      mma_commit(done);
+    }
+  } else {
+    // ---- epilogue: 8 warps; TMEM lane quarter q = warp % 4, column half h.
+    // Each chunk's TMEM partial is added into fp32 registers with
+    // round-to-nearest, so the tensor core's internal accumulation only ever
+    // spans CHUNK_KB*16 terms.
+    const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
+    float acc[BN / 2];
+#pragma unroll
+    for (int j = 0; j < BN / 2; ++j) acc[j] = 0.0f;
+    bool ok = true;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    for (int c = 0; c < nchunks; ++c) {
+      const int b = c & 1;
+      bool w = wait_bounded(accf0 + 8 * b, (c >> 1) & 1, limit, abort_flag);
+      w = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
+      if (!w) {
+        ok = false;
+        if (lane == 0) *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t t0 = tmem + lane_base + (uint32_t)(b * BN + h * (BN / 2));
+#pragma unroll
+      for (int i = 0; i < BN / 64; ++i) {
+        uint32_t r[32];
+        tmem_ld32(t0 + i * 32, r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[i * 32 + j] = __fadd_rn(acc[i * 32 + j], __uint_as_float(r[j]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce0 + 8 * b);
+    }
+    if (ok) {
+      const int64_t row = m0 + q * 32 + lane;
+      if (row < M) {
+        const int64_t nb = n0 + h * (BN / 2);
+        float* dst = C + row + nb * ldc;
+#pragma unroll
+        for (int j = 0; j < BN / 2; ++j)
+          if (nb + j < N) __stcs(dst + (int64_t)j * ldc, acc[j]);
+      }
+    } else {
+      atomicOr(err, mk::ERRBIT_TIMEOUT);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    // every issued MMA has completed before the columns are released
+    volatile int no_abort = 0;
+    wait_bounded(done, 0, limit, &no_abort);
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ------------------------------------------------------------- host --------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// Row-major (rows x cols) fp32 panel, boxes of box_rows x 32 with 128B swizzle.
+int make_map(CUtensorMap* map, const float* base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
+  auto enc = encode_fn();
+  if (!enc) return mk::fail(MK_ERR_CUDA, "mk_sgemm_3xtf32: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 4};
+  cuuint32_t box[2] = {(cuuint32_t)ROWF, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return mk::fail(MK_ERR_CUDA, "mk_sgemm_3xtf32: cuTensorMapEncodeTiled failed");
+  return MK_OK;
+}
+
+std::once_flag g_attr_once;
+cudaError_t g_attr_err = cudaSuccess;
+
+}  // namespace
+
+extern "C" int mk_sgemm_3xtf32(float* C, const float* A, const float* B, int64_t M, int64_t N, int64_t K,
+                               int64_t lda, int64_t ldb, int64_t ldc, void* stream) {
+  MK_ENTRY_DEVICE(dev);
+  if (M < 0 || N < 0 || K < 0) return mk::fail(MK_ERR_INVALID, "mk_sgemm_3xtf32: negative size");
+  if (M == 0 || N == 0) return MK_OK;
+  if (lda < M || ldb < K || ldc < M || lda < 1 || ldb < 1)
+    return mk::fail(MK_ERR_INVALID, "mk_sgemm_3xtf32: leading dimension too small");
+  const int64_t Kt = (K / KB) * KB;
+  if (!C || (Kt > 0 && (!A || !B))) return mk::fail(MK_ERR_INVALID, "mk_sgemm_3xtf32: null pointer");
+  if (mk::cdiv(M, BM) > 65535 || M > INT32_MAX || N > INT32_MAX || Kt / KB > 65535)
+    return mk::fail(MK_ERR_INVALID, "mk_sgemm_3xtf32: problem too large");
+  cudaStream_t s = mk::as_stream(stream);
+  if (Kt == 0) {
+    cudaError_t e = cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)M * 4, (size_t)N, s);
+    return e == cudaSuccess ? MK_OK : mk::fail_cuda(e, "mk_sgemm_3xtf32: zero fill");
+  }
+  const int nkb = (int)(Kt / KB);
+  const uint64_t cols = (uint64_t)nkb * ROWF;
+  const size_t a_bytes = (((size_t)M * cols * 4) + 1023) & ~(size_t)1023;
+  const size_t b_bytes = (size_t)N * cols * 4;
+  void* ws = nullptr;
+  int rc = mk::stream_workspace(dev, s, a_bytes + b_bytes, &ws);
+  if (rc != MK_OK) return rc;
+  float* A2 = static_cast<float*>(ws);
+  float* B2 = reinterpret_cast<float*>(static_cast<char*>(ws) + a_bytes);
+
+  split_a<<<dim3((unsigned)mk::cdiv(M, 64), (unsigned)nkb), 256, 0, s>>>(A2, A, M, lda, nkb);
+  {
+    const int64_t total = N * (int64_t)cols;
+    int64_t blocks = mk::cdiv(total, 256);
+    const int64_t cap = (int64_t)dev->sms * 8;
+    split_b<<<(unsigned)(blocks > cap ? cap : blocks), 256, 0, s>>>(B2, B, N, ldb, nkb);
+  }
+  CUtensorMap mapA, mapB;
+  if ((rc = make_map(&mapA, A2, cols, (uint64_t)M, BM)) != MK_OK) return rc;
+  if ((rc = make_map(&mapB, B2, cols, (uint64_t)N, BN)) != MK_OK) return rc;
+  std::call_once(g_attr_once, [] {
+    g_attr_err = cudaFuncSetAttribute(sgemm_tf32x3, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  });
+  if (g_attr_err != cudaSuccess) return mk::fail_cuda(g_attr_err, "mk_sgemm_3xtf32: cudaFuncSetAttribute");
+  dim3 grid((unsigned)mk::cdiv(N, BN), (unsigned)mk::cdiv(M, BM));
+  sgemm_tf32x3<<<grid, kThreads, SMEM_BYTES, s>>>(mapA, mapB, C, M, N, ldc, nkb, mk::wait_limit_cycles(),
+                                                   dev->err_word);
+  return mk::check_launch("mk_sgemm_3xtf32: launch");
+}

@@ -15,7 +15,8 @@ kernel             reference definition                        C entry point
 ``vadd``           test/test_gpu_simt.jl:13-16                 mk_vadd_f32
 ``gather``         ``c[i] = a[idx[i]]`` (src/lower.jl:4031)    mk_gather_f32
 ``histogram``      test/test_ka_cpu.jl:16-19, test_gpu_simt:49  mk_hist_u32
-``mm_tiled``       examples/tiled_matmul.jl:28-48              mk_matmul_tiled16_f32
+``mm_tiled``       examples/tiled_matmul.jl:28-48              mk_sgemm_3xtf32
+``mm_tiled_simt``  examples/tiled_matmul.jl:28-48 (SIMT)       mk_matmul_tiled16_f32
 =================  =========================================  ===========================
 
 The launch is asynchronous; ``synchronize(backend)`` waits and raises
@@ -174,6 +175,13 @@ def _matmul_operands(args, nd, what):
     return Cm, A, B, M, N, K
 
 
+def _launch_mm_tiled(args, nd, wg, stream) -> None:
+    Cm, A, B, M, N, K = _matmul_operands(args, nd, "mm_tiled!")
+    _lib.check(_lib.lib().mk_sgemm_3xtf32(
+        Cm.pointer(), A.pointer(), B.pointer(), M, N, K, A.size(1), B.size(1), Cm.size(1), stream),
+        "mm_tiled!")
+
+
 def _launch_mm_tiled_simt(args, nd, wg, stream) -> None:
     Cm, A, B, M, N, K = _matmul_operands(args, nd, "mm_tiled!")
     _lib.check(_lib.lib().mk_matmul_tiled16_f32(
@@ -184,5 +192,7 @@ def _launch_mm_tiled_simt(args, nd, wg, stream) -> None:
 vadd = KernelFunction("vadd!", 1, _launch_vadd)
 gather = KernelFunction("gather!", 1, _launch_gather)
 histogram = KernelFunction("histogram!", 1, _launch_histogram)
+# mm_tiled! on the tcgen05 tensor cores in 3xTF32 (the hot path).
+mm_tiled = KernelFunction("mm_tiled!", 2, _launch_mm_tiled, static_wg=(16, 16))
 # The reference's 16x16 @localmem kernel run on CUDA cores (SIMT comparison point).
 mm_tiled_simt = KernelFunction("mm_tiled!", 2, _launch_mm_tiled_simt, static_wg=(16, 16))

@@ -126,6 +126,20 @@ MK_API int mk_gather_f32(float* c, const float* a, int64_t na, const int32_t* id
 MK_API int mk_hist_u32(uint32_t* counts, int32_t nbins, const int32_t* keys1, int64_t n,
                 void* stream);
 
+/* C[M,N] = A[M,K] * B[K,N], column-major with leading dimensions lda>=M,
+ * ldb>=K, ldc>=M, fp32 in/out.  Computed on the tcgen05 tensor cores in 3xTF32
+ * split precision (a_hi*b_hi + a_hi*b_lo + a_lo*b_hi, fp32 accumulation in
+ * TMEM): within ~1e-6 relative (Frobenius) of an fp64 product for K=8192.
+ * Only the first 16*floor(K/16) columns of A / rows of B take part, as in the
+ * reference tiled kernel, which ignores the K % 16 remainder
+ * (examples/tiled_matmul.jl:34).  Replaces mm_tiled! launches
+ * (examples/tiled_matmul.jl:28-48).  Row-major callers compute C^T = B^T A^T by
+ * swapping operands.  Uses a per-stream device workspace of (M+N)*2*K*4 bytes
+ * for the split operands (allocated on first use, grown as needed). */
+MK_API int mk_sgemm_3xtf32(float* C, const float* A, const float* B,
+                           int64_t M, int64_t N, int64_t K,
+                           int64_t lda, int64_t ldb, int64_t ldc, void* stream);
+
 /* The reference's own algorithm on CUDA cores: one output per thread, 16x16
  * shared-memory tiles, K % 16 ignored (examples/tiled_matmul.jl:28-48).  Kept
  * as the SIMT comparison point for the tensor-core path; same argument rules. */
