@@ -361,7 +361,8 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
 
         def __init__(self):
             super().__init__(rank, world)
-            m, n, k = self.m, self.nn, self.k = self.cfg["m"], self.cfg["n"], self.cfg["k"]
+            m, n, k = self.m, self.nn, self.k = ((n_override,) * 3 if n_override
+                                                 else (self.cfg["m"], self.cfg["n"], self.cfg["k"]))
             self.A_host = workloads.normal((m, k), stream=40 + 100 * rank)
             self.B_host = workloads.normal((k, n), stream=41)
             self.A, self.B = mk.MLIRArray(self.A_host), mk.MLIRArray(self.B_host)
@@ -380,7 +381,7 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
 
         def check(self):
             import oracle
-            ii = np.array([0, 1, 4095, 8191]); jj = np.array([0, 8191, 17, 4000])
+            ii = np.array([0, 1, self.m // 2, self.m - 1]); jj = np.array([0, self.nn - 1, 17, self.nn // 2])
             got = mk.Array(self.C)[ii, jj]
             want = oracle.matmul_entries_f64(self.A_host, self.B_host, ii, jj)
             np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-3)
@@ -415,7 +416,8 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
 
         def __init__(self):
             super().__init__(rank, world)
-            m, n, k = self.m, self.nn, self.k = self.cfg["m"], self.cfg["n"], self.cfg["k"]
+            m, n, k = self.m, self.nn, self.k = ((n_override,) * 3 if n_override
+                                                 else (self.cfg["m"], self.cfg["n"], self.cfg["k"]))
             self.A_host = workloads.normal((m, k), stream=40 + 100 * rank)
             self.B_host = workloads.normal((k, n), stream=41)
             self.A, self.B = mk.MLIRArray(self.A_host), mk.MLIRArray(self.B_host)
@@ -434,7 +436,7 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
 
         def check(self):
             import oracle
-            ii = np.array([0, 1, 4095, 8191]); jj = np.array([0, 8191, 17, 4000])
+            ii = np.array([0, 1, self.m // 2, self.m - 1]); jj = np.array([0, self.nn - 1, 17, self.nn // 2])
             got = mk.Array(self.C)[ii, jj]
             want = oracle.matmul_entries_f64(self.A_host, self.B_host, ii, jj)
             np.testing.assert_allclose(got, want, rtol=1e-4, atol=2e-4)

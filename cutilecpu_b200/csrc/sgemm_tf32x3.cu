@@ -153,45 +153,70 @@ __device__ __forceinline__ float tf32_rna(float x) {
 
 // ------------------------------------------------------------- split -------
 
-// A (M x K column-major, lda) -> A2 (M rows x 2Kt, row-major): one block per
-// 64 rows x one 16-wide k-block, transposed through shared memory.
+__device__ __forceinline__ float4 hi4(float4 x) {
+  return make_float4(tf32_rna(x.x), tf32_rna(x.y), tf32_rna(x.z), tf32_rna(x.w));
+}
+__device__ __forceinline__ float4 lo4(float4 x, float4 h) {
+  return make_float4(tf32_rna(x.x - h.x), tf32_rna(x.y - h.y), tf32_rna(x.z - h.z), tf32_rna(x.w - h.w));
+}
+
+// Output segment layout: each (row, k-block) owns 8 float4 = one 128-byte
+// line: float4 i < 4 holds hi of source float4 i, float4 4 + i its lo.  Eight
+// consecutive lanes build one segment, one float4 each, so every warp store
+// covers four whole lines.
+__device__ __forceinline__ float4 segment_part(float4 x, int i) {
+  const float4 h = hi4(x);
+  return i < 4 ? h : lo4(x, h);
+}
+
+// A (M x K column-major, lda) -> A2 (M rows x 2Kt, row-major).  One block per
+// 128 rows x 2 k-blocks: the 32 source columns are read coalesced into shared
+// memory (the transpose), then written as whole 128-byte segments.
+constexpr int SA_ROWS = 128;
+constexpr int SA_KBS = 2;
 __global__ void __launch_bounds__(256) split_a(float* __restrict__ A2, const float* __restrict__ A, int64_t M,
                                                int64_t lda, int nkb) {
-  __shared__ float t[KB][65];
-  const int64_t m0 = (int64_t)blockIdx.x * 64;
-  const int kb = blockIdx.y;
-  for (int e = threadIdx.x; e < KB * 64; e += 256) {
-    const int kk = e >> 6, mm = e & 63;
+  __shared__ float t[SA_KBS * KB][SA_ROWS + 1];
+  const int64_t m0 = (int64_t)blockIdx.x * SA_ROWS;
+  const int kb0 = blockIdx.y * SA_KBS;
+  const int nk = min(SA_KBS, nkb - kb0) * KB;
+  for (int e = threadIdx.x; e < SA_KBS * KB * SA_ROWS; e += 256) {
+    const int kk = e / SA_ROWS, mm = e % SA_ROWS;
     const int64_t m = m0 + mm;
-    t[kk][mm] = (m < M) ? A[m + (int64_t)(kb * KB + kk) * lda] : 0.0f;
+    t[kk][mm] = (kk < nk && m < M) ? A[m + (int64_t)(kb0 * KB + kk) * lda] : 0.0f;
   }
   __syncthreads();
   const int64_t row_len = (int64_t)nkb * ROWF;
-  for (int e = threadIdx.x; e < 64 * ROWF; e += 256) {
-    const int mm = e >> 5, j = e & 31;
+#pragma unroll
+  for (int it = 0; it < SA_ROWS * SA_KBS * 8 / 256; ++it) {
+    const int f = it * 256 + threadIdx.x;
+    const int seg = f >> 3, i = f & 7;
+    const int j = seg % SA_KBS, mm = seg / SA_KBS;  // consecutive segments: adjacent k-blocks of a row
     const int64_t m = m0 + mm;
-    if (m < M) {
-      const float x = t[j & 15][mm];
-      const float hi = tf32_rna(x);
-      A2[m * row_len + (int64_t)kb * ROWF + j] = (j < KB) ? hi : tf32_rna(x - hi);
+    if (m < M && j * KB < nk) {
+      const int k = j * KB + 4 * (i & 3);
+      const float4 x = make_float4(t[k][mm], t[k + 1][mm], t[k + 2][mm], t[k + 3][mm]);
+      reinterpret_cast<float4*>(A2 + m * row_len + (int64_t)(kb0 + j) * ROWF)[i] = segment_part(x, i);
     }
   }
 }
 
-// B (K x N column-major, ldb) -> B2 (N rows x 2Kt): already K-major; B2 is
-// written linearly.
+// B (K x N column-major, ldb) -> B2 (N rows x 2Kt): already K-major, so B2 is
+// written linearly, 8 lanes per (column n, k-block) segment.  VEC: B and ldb
+// allow 16-byte loads.
+template <bool VEC>
 __global__ void __launch_bounds__(256) split_b(float* __restrict__ B2, const float* __restrict__ B, int64_t N,
                                                int64_t ldb, int nkb) {
-  const int64_t total = N * (int64_t)nkb * ROWF;
+  const int64_t total = N * (int64_t)nkb * 8;  // float4 outputs
   const int64_t stride = (int64_t)gridDim.x * 256;
-  for (int64_t e = (int64_t)blockIdx.x * 256 + threadIdx.x; e < total; e += stride) {
-    const int j = (int)(e & 31);
-    const int64_t t = e >> 5;
-    const int kb = (int)(t % nkb);
-    const int64_t n = t / nkb;
-    const float x = B[(int64_t)kb * KB + (j & 15) + n * ldb];
-    const float hi = tf32_rna(x);
-    B2[e] = (j < KB) ? hi : tf32_rna(x - hi);
+  for (int64_t t = (int64_t)blockIdx.x * 256 + threadIdx.x; t < total; t += stride) {
+    const int64_t seg = t >> 3;
+    const int i = (int)(t & 7);
+    const int64_t n = seg / nkb;
+    const int kb = (int)(seg - n * nkb);
+    const float* src = B + n * ldb + (int64_t)kb * KB + 4 * (i & 3);
+    const float4 x = VEC ? *reinterpret_cast<const float4*>(src) : make_float4(src[0], src[1], src[2], src[3]);
+    reinterpret_cast<float4*>(B2)[t] = segment_part(x, i);
   }
 }
 
@@ -418,7 +443,7 @@ extern "C" int mk_sgemm_3xtf32(float* C, const float* A, const float* B, int64_t
     return mk::fail(MK_ERR_INVALID, "mk_sgemm_3xtf32: leading dimension too small");
   const int64_t Kt = (K / KB) * KB;
   if (!C || (Kt > 0 && (!A || !B))) return mk::fail(MK_ERR_INVALID, "mk_sgemm_3xtf32: null pointer");
-  if (mk::cdiv(M, BM) > 65535 || M > INT32_MAX || N > INT32_MAX || Kt / KB > 65535)
+  if (mk::cdiv(M, BM) > 65535 || M > INT32_MAX || N > INT32_MAX || mk::cdiv(Kt / KB, SA_KBS) > 65535)
     return mk::fail(MK_ERR_INVALID, "mk_sgemm_3xtf32: problem too large");
   cudaStream_t s = mk::as_stream(stream);
   if (Kt == 0) {
@@ -435,12 +460,16 @@ extern "C" int mk_sgemm_3xtf32(float* C, const float* A, const float* B, int64_t
   float* A2 = static_cast<float*>(ws);
   float* B2 = reinterpret_cast<float*>(static_cast<char*>(ws) + a_bytes);
 
-  split_a<<<dim3((unsigned)mk::cdiv(M, 64), (unsigned)nkb), 256, 0, s>>>(A2, A, M, lda, nkb);
+  split_a<<<dim3((unsigned)mk::cdiv(M, SA_ROWS), (unsigned)mk::cdiv(nkb, SA_KBS)), 256, 0, s>>>(A2, A, M, lda, nkb);
   {
-    const int64_t total = N * (int64_t)cols;
+    const int64_t total = N * (int64_t)nkb * 8;
     int64_t blocks = mk::cdiv(total, 256);
     const int64_t cap = (int64_t)dev->sms * 8;
-    split_b<<<(unsigned)(blocks > cap ? cap : blocks), 256, 0, s>>>(B2, B, N, ldb, nkb);
+    if (blocks > cap) blocks = cap;
+    if (mk::aligned16(B) && ldb % 4 == 0)
+      split_b<true><<<(unsigned)blocks, 256, 0, s>>>(B2, B, N, ldb, nkb);
+    else
+      split_b<false><<<(unsigned)blocks, 256, 0, s>>>(B2, B, N, ldb, nkb);
   }
   CUtensorMap mapA, mapB;
   if ((rc = make_map(&mapA, A2, cols, (uint64_t)M, BM)) != MK_OK) return rc;
