@@ -56,6 +56,7 @@ constexpr int EPI_WARPS = 8;
 constexpr int kThreads = 32 * (2 + EPI_WARPS);  // producer, MMA, 8 epilogue warps
 constexpr int CHUNK_KB = 8;                      // k-blocks per TMEM accumulation chunk (128 k)
 constexpr uint32_t TMEM_COLS = 2 * BN;           // two 256-column accumulators
+constexpr int GROUP_M = 16;                      // tile-rows per raster group
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 
 // kind::tf32 instruction descriptor: D f32, A/B tf32, both K-major, M=128, N=256.
@@ -239,8 +240,19 @@ sgemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t m0 = (int64_t)blockIdx.y * BM;
-  const int64_t n0 = (int64_t)blockIdx.x * BN;
+  // Grouped raster: consecutive CTAs walk GROUP_M tile-rows column by column,
+  // so a wave of ~148 CTAs shares ~16 A panels and ~9 B panels in L2.
+  int64_t m0, n0;
+  {
+    const int nM = (int)((M + BM - 1) / BM), nN = (int)((N + BN - 1) / BN);
+    const int t = blockIdx.x;
+    const int per_group = GROUP_M * nN;
+    const int first_m = (t / per_group) * GROUP_M;
+    const int gsize = min(GROUP_M, nM - first_m);
+    const int r = t % per_group;
+    m0 = (int64_t)(first_m + r % gsize) * BM;
+    n0 = (int64_t)(r / gsize) * BN;
+  }
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
   const uint32_t accf0 = smem_u32(bars + 2 * STAGES), acce0 = smem_u32(bars + 2 * STAGES + 2);
   const uint32_t done = smem_u32(bars + 2 * STAGES + 4);
@@ -443,7 +455,7 @@ extern "C" int mk_sgemm_3xtf32(float* C, const float* A, const float* B, int64_t
     return mk::fail(MK_ERR_INVALID, "mk_sgemm_3xtf32: leading dimension too small");
   const int64_t Kt = (K / KB) * KB;
   if (!C || (Kt > 0 && (!A || !B))) return mk::fail(MK_ERR_INVALID, "mk_sgemm_3xtf32: null pointer");
-  if (mk::cdiv(M, BM) > 65535 || M > INT32_MAX || N > INT32_MAX || mk::cdiv(Kt / KB, SA_KBS) > 65535)
+  if (mk::cdiv(M, BM) * mk::cdiv(N, BN) > INT32_MAX || M > INT32_MAX || N > INT32_MAX || mk::cdiv(Kt / KB, SA_KBS) > 65535)
     return mk::fail(MK_ERR_INVALID, "mk_sgemm_3xtf32: problem too large");
   cudaStream_t s = mk::as_stream(stream);
   if (Kt == 0) {
@@ -478,7 +490,8 @@ extern "C" int mk_sgemm_3xtf32(float* C, const float* A, const float* B, int64_t
     g_attr_err = cudaFuncSetAttribute(sgemm_tf32x3, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   });
   if (g_attr_err != cudaSuccess) return mk::fail_cuda(g_attr_err, "mk_sgemm_3xtf32: cudaFuncSetAttribute");
-  dim3 grid((unsigned)mk::cdiv(N, BN), (unsigned)mk::cdiv(M, BM));
+  const int64_t tiles = mk::cdiv(N, BN) * mk::cdiv(M, BM);
+  dim3 grid((unsigned)tiles);
   sgemm_tf32x3<<<grid, kThreads, SMEM_BYTES, s>>>(mapA, mapB, C, M, N, ldc, nkb, mk::wait_limit_cycles(),
                                                    dev->err_word);
   return mk::check_launch("mk_sgemm_3xtf32: launch");
