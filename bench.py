@@ -559,6 +559,7 @@ def run_ours(kind: str, args, rank: int, world: int, local_rank: int) -> dict | 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle
+        oracle.lib().or_set_num_threads(host_threads())
         fn, units, sample = w.cpu_sample(oracle.num_threads())
         t, reps = time_cpu(fn, budget_s=args.cpu_budget)
         cpu = {"value": round(units / t / (1e12 if w.unit == "TFLOP/s" else 1e9), 3), "unit": w.unit,
@@ -612,12 +613,22 @@ PROFILED_TRAFFIC: dict[str, float | None] = {
 }
 
 
-def run_reference(kind: str, args) -> dict:
+def host_threads() -> int:
+    """All host threads this process may use (torchrun sets OMP_NUM_THREADS=1
+    for its workers, so the OpenMP default is not trusted)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference(kind: str, args, world: int = 1) -> dict:
     """The reference's CPU implementation of the path (restated MLIRBackend)."""
     import oracle
 
     from cutilecpu_b200 import workloads
 
+    oracle.lib().or_set_num_threads(host_threads())
     threads = oracle.num_threads()
     cfg = workloads.CONFIGS
     L = oracle.lib()
@@ -671,7 +682,7 @@ def run_reference(kind: str, args) -> dict:
     dt = (time.perf_counter() - t0) / args.steps
     scale = 1e12 if unit == "TFLOP/s" else 1e9
     v = round(units / dt / scale, 3)
-    return {"metric": metric, "value": v, "unit": unit, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+    return {"metric": metric, "value": v, "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded numpy Philox, host-generated)", "impl": "reference",
             "config": {"workload": conf, "parallelism": "host OpenMP"},
@@ -709,7 +720,7 @@ def main():
         if args.warmup is None:
             args.warmup = 1
         for k in kinds:
-            print(json.dumps(run_reference(k, args)), flush=True)
+            print(json.dumps(run_reference(k, args, world)), flush=True)
         return
 
     import torch
