@@ -9,7 +9,7 @@ from ._lib import KernelException, MLIRKernelsError
 from .array import (Array, MLIRArray, MLIRCUDABackend, allocate, copyto, functional, get_backend,
                     launch_config, ones, supports_atomics, synchronize, zeros)
 from .kernels import Kernel, KernelFunction, gather, histogram, mm_tiled, mm_tiled_simt, vadd
-from .reductions import (Broadcasted, abs2, count, identity, mapreduce, mapreducedim, maximum, minimum,
+from .reductions import (Broadcasted, abs2, accumulate, cumsum, count, identity, mapreduce, mapreducedim, maximum, minimum,
                      positive, prod, reduce, sum)
 from . import distributed, reductions
 
@@ -17,6 +17,6 @@ __all__ = [
     "KernelException", "MLIRKernelsError", "Array", "MLIRArray", "MLIRCUDABackend", "allocate",
     "copyto", "functional", "get_backend", "launch_config", "ones", "supports_atomics", "synchronize",
     "zeros", "Kernel", "KernelFunction", "gather", "histogram", "mm_tiled", "mm_tiled_simt", "vadd", "Broadcasted",
-    "abs2", "count", "identity", "mapreduce", "mapreducedim", "maximum", "minimum", "positive", "prod",
+    "abs2", "accumulate", "cumsum", "count", "identity", "mapreduce", "mapreducedim", "maximum", "minimum", "positive", "prod",
     "reduce", "sum", "distributed",
 ]

@@ -32,6 +32,8 @@ SIGNATURES = {
     "mk_mapreduce_f32": (_int, [_vp, _vp, _i64, _int, _int, _f64, _vp]),
     "mk_sum_sq_f32": (_int, [_vp, _vp, _i64, _vp]),
     "mk_mapreduce_f32_noalloc": (_int, [_vp, _vp, _i64, _int, _int, _f64, _vp]),
+    "mk_mapreduce_dim_f32": (_int, [_vp, _vp, _i64, _i64, _i64, _int, _int, _f64, _vp]),
+    "mk_accumulate_f32": (_int, [_vp, _vp, _i64, _int, _f64, _int, _vp]),
     "mk_gather_f32": (_int, [_vp, _vp, _i64, _vp, _i64, _vp]),
     "mk_hist_u32": (_int, [_vp, _i32, _vp, _i64, _vp]),
     "mk_sgemm_3xtf32": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),

@@ -8,6 +8,7 @@
 #include <stdlib.h>
 
 #include <map>
+#include <tuple>
 #include <mutex>
 #include <utility>
 
@@ -28,7 +29,7 @@ struct Workspace {
   void* ptr = nullptr;
   size_t bytes = 0;
 };
-static std::map<std::pair<int, cudaStream_t>, Workspace> g_workspace;
+static std::map<std::tuple<int, cudaStream_t, int>, Workspace> g_workspace;
 
 int fail(int code, const std::string& msg) {
   t_last_error = msg;
@@ -112,9 +113,9 @@ int reduce_scratch(Device* d, cudaStream_t s, ReduceScratch* out) {
   return MK_OK;
 }
 
-int stream_workspace(Device* d, cudaStream_t s, size_t bytes, void** out) {
+int stream_workspace(Device* d, cudaStream_t s, size_t bytes, void** out, int slot) {
   std::lock_guard<std::mutex> lk(g_mu);
-  Workspace& w = g_workspace[std::make_pair(d->id, s)];
+  Workspace& w = g_workspace[std::make_tuple(d->id, s, slot)];
   if (w.bytes < bytes) {
     if (w.ptr) {
       // the old buffer may still be read by work queued on this stream

@@ -25,49 +25,14 @@
 #include <string>
 
 #include "mk_common.cuh"
+#include "reduce_ops.cuh"
 
 namespace {
 
+using namespace mk::rops;
+
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;  // float4 loads in flight per thread
-
-__device__ __forceinline__ float mapf(int f, float v) {
-  switch (f) {
-    case MK_F_ABS2: return __fmul_rn(v, v);
-    case MK_F_ABS: return fabsf(v);
-    case MK_F_GT0: return v > 0.0f ? 1.0f : 0.0f;
-    default: return v;
-  }
-}
-
-__device__ __forceinline__ double jl_max(double a, double b) {
-  if (a != a) return a;
-  if (b != b) return b;
-  if (a == b) return signbit(a) ? b : a;
-  return a > b ? a : b;
-}
-__device__ __forceinline__ double jl_min(double a, double b) {
-  if (a != a) return a;
-  if (b != b) return b;
-  if (a == b) return signbit(a) ? a : b;
-  return a < b ? a : b;
-}
-
-template <int OP>
-__device__ __forceinline__ double combine(double a, double b) {
-  if (OP == MK_OP_ADD) return a + b;
-  if (OP == MK_OP_MUL) return a * b;
-  if (OP == MK_OP_MAX) return jl_max(a, b);
-  return jl_min(a, b);
-}
-
-template <int OP>
-__device__ __forceinline__ double neutral() {
-  if (OP == MK_OP_ADD) return 0.0;
-  if (OP == MK_OP_MUL) return 1.0;
-  if (OP == MK_OP_MAX) return -INFINITY;
-  return INFINITY;
-}
 
 // Fold one float4 (already mapped) into the thread accumulator.
 template <int F, int OP>

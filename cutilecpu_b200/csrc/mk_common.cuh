@@ -43,10 +43,12 @@ struct ReduceScratch {
 };
 int reduce_scratch(Device* d, cudaStream_t s, ReduceScratch* out);
 
-// Growable device workspace private to one (device, stream) pair, for kernels
-// that stage re-laid-out operands (the 3xTF32 GEMM's hi/lo panels).  Grows with
-// cudaMalloc (after a cudaFree of the smaller buffer); never shrinks.
-int stream_workspace(Device* d, cudaStream_t s, size_t bytes, void** out);
+// Growable device workspace private to one (device, stream, slot), for kernels
+// that stage re-laid-out operands (the 3xTF32 GEMM's hi/lo panels) or keep
+// per-tile state (scan, dims reductions).  Grows with cudaMalloc (after a
+// cudaFree of the smaller buffer, once the stream has drained); never shrinks.
+enum : int { WS_GEMM = 0, WS_SCAN = 1, WS_DIMS = 2 };
+int stream_workspace(Device* d, cudaStream_t s, size_t bytes, void** out, int slot);
 
 // Bounded device waits give up after this many SM clock cycles (env
 // MK_WAIT_LIMIT_CYCLES overrides; default ~2 s at 1.9 GHz).

@@ -467,7 +467,7 @@ extern "C" int mk_sgemm_3xtf32(float* C, const float* A, const float* B, int64_t
   const size_t a_bytes = (((size_t)M * cols * 4) + 1023) & ~(size_t)1023;
   const size_t b_bytes = (size_t)N * cols * 4;
   void* ws = nullptr;
-  int rc = mk::stream_workspace(dev, s, a_bytes + b_bytes, &ws);
+  int rc = mk::stream_workspace(dev, s, a_bytes + b_bytes, &ws, mk::WS_GEMM);
   if (rc != MK_OK) return rc;
   float* A2 = static_cast<float*>(ws);
   float* B2 = reinterpret_cast<float*>(static_cast<char*>(ws) + a_bytes);

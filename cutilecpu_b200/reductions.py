@@ -15,6 +15,7 @@ and min are exact.  The result is returned to the host as a Python number.
 """
 from __future__ import annotations
 
+import math
 import operator
 
 import torch
@@ -96,34 +97,66 @@ def mapreduce_device(f, op, src, init=None, out: torch.Tensor | None = None) -> 
     return out
 
 
-def mapreduce(f, op, src, init=None, neutral=None):
-    """``AK.mapreduce(f, op, src; init, neutral)`` / Base ``mapreduce``."""
+def mapreduce_dims_into(f, op, R: MLIRArray, A, dim: int, init=None) -> MLIRArray:
+    """Reduce the 1-based dimension ``dim`` of ``A`` into ``R`` (Float32, same
+    dims as ``A`` with ``size(R, dim) == 1``): one ``mk_mapreduce_dim_f32``."""
+    f, A = _unwrap(f, A)
+    fname, opname = _f_name(f), _op_name(op)
+    if not 1 <= dim <= max(1, A.ndims):
+        raise _lib.MLIRKernelsError(f"MLIRCUDABackend: dims={dim} out of range for {A.dims}")
+    if R.eltype != "Float32":
+        raise _lib.MLIRKernelsError(f"mapreducedim!: dims result eltype {R.eltype} unsupported")
+    pre = math.prod(A.dims[:dim - 1])
+    ln = A.dims[dim - 1] if dim <= A.ndims else 1
+    post = math.prod(A.dims[dim:])
+    if R.length != pre * post:
+        raise _lib.MLIRKernelsError(f"mapreducedim!: result dims {R.dims} do not match reducing {A.dims} over {dim}")
+    init_v = _NEUTRAL[opname] if init is None else float(init)
+    _lib.check(_lib.lib().mk_mapreduce_dim_f32(R.pointer(), A.pointer(), pre, ln, post, _lib.MK_F[fname],
+                                               _lib.MK_OP[opname], init_v, current_stream_handle()),
+               "mapreducedim!")
+    return R
+
+
+def _dims_result(f, op, A, dims: int, init=None) -> MLIRArray:
+    from .array import MLIRCUDABackend, allocate
+    _, src = _unwrap(f, A)
+    rdims = tuple(1 if d == dims - 1 else n for d, n in enumerate(src.dims))
+    R = allocate(MLIRCUDABackend(), "Float32", rdims)
+    return mapreduce_dims_into(f, op, R, A, dims, init)
+
+
+def mapreduce(f, op, src, init=None, neutral=None, dims=None):
+    """``AK.mapreduce(f, op, src; init, neutral, dims)`` / Base ``mapreduce``:
+    a number, or with ``dims`` an MLIRArray with that dimension reduced."""
     del neutral  # the kernel uses op's own identity element
+    if dims is not None:
+        return _dims_result(f, op, src, dims, init)
     return mapreduce_device(f, op, src, init).item()
 
 
-def reduce(op, src, init=None, neutral=None):
-    """``AK.reduce(op, src; init)``."""
-    return mapreduce(identity, op, src, init=init, neutral=neutral)
+def reduce(op, src, init=None, neutral=None, dims=None):
+    """``AK.reduce(op, src; init, dims)``."""
+    return mapreduce(identity, op, src, init=init, neutral=neutral, dims=dims)
 
 
-def sum(f_or_src, src=None):
-    """``sum(x)`` or ``sum(f, x)``."""
+def sum(f_or_src, src=None, dims=None):
+    """``sum(x)``, ``sum(f, x)`` or with ``dims=d``."""
     if src is None:
-        return mapreduce(identity, operator.add, f_or_src)
-    return mapreduce(f_or_src, operator.add, src)
+        return mapreduce(identity, operator.add, f_or_src, dims=dims)
+    return mapreduce(f_or_src, operator.add, src, dims=dims)
 
 
-def prod(src):
-    return mapreduce(identity, operator.mul, src)
+def prod(src, dims=None):
+    return mapreduce(identity, operator.mul, src, dims=dims)
 
 
-def maximum(src):
-    return mapreduce(identity, max, src)
+def maximum(src, dims=None):
+    return mapreduce(identity, max, src, dims=dims)
 
 
-def minimum(src):
-    return mapreduce(identity, min, src)
+def minimum(src, dims=None):
+    return mapreduce(identity, min, src, dims=dims)
 
 
 def count(pred, src) -> int:
@@ -134,14 +167,40 @@ def count(pred, src) -> int:
 
 
 def mapreducedim(f, op, R: MLIRArray, A, init=None) -> MLIRArray:
-    """``GPUArrays.mapreducedim!(f, op, R, A; init)`` for a full reduction
-    (``length(R) == 1``), the form ``sum``/``mapreduce`` reach: the result is
-    written into ``R`` on the device, with no host round trip."""
-    if R.length != 1:
-        raise _lib.MLIRKernelsError(
-            "MLIRCUDABackend.mapreducedim!: only full reductions (length(R) == 1) are supported")
+    """``GPUArrays.mapreducedim!(f, op, R, A; init)``.  A full reduction
+    (``length(R) == 1``) is one fused launch written into ``R`` on the device;
+    otherwise exactly one dimension may be reduced (the reference allows only
+    single-dim reductions too, ext/MLIRCUDAExt.jl:115-117)."""
     if R.eltype not in ("Float32", "Float64"):
         raise _lib.MLIRKernelsError(f"mapreducedim!: result eltype {R.eltype} unsupported")
-    res = mapreduce_device(f, op, A, init)
-    R.storage.copy_(res.to(R.storage.dtype))
-    return R
+    _, src = _unwrap(f, A)
+    if R.length == 1 and src.length != 1:
+        res = mapreduce_device(f, op, A, init)
+        R.storage.copy_(res.to(R.storage.dtype))
+        return R
+    rd = tuple(d + 1 for d in range(src.ndims) if R.size(d + 1) == 1 and src.size(d + 1) != 1)
+    if len(rd) != 1:
+        raise _lib.MLIRKernelsError(f"MLIRCUDABackend.mapreducedim!: only single-dim reductions (got dims={rd})")
+    return mapreduce_dims_into(f, op, R, A, rd[0], init)
+
+
+def accumulate(op, dst: MLIRArray, src: MLIRArray, init=None, inclusive: bool = True) -> MLIRArray:
+    """``AK.accumulate!(op, dst, src; init, inclusive)``: prefix scan of a
+    Float32 vector into ``dst`` (which may be ``src``) in one launch."""
+    for name, a in (("dst", dst), ("src", src)):
+        if not isinstance(a, MLIRArray) or a.eltype != "Float32":
+            raise _lib.MLIRKernelsError(f"accumulate!: `{name}` must be a Float32 MLIRArray")
+    if dst.length < src.length:
+        raise _lib.MLIRKernelsError("accumulate!: dst is shorter than src")
+    opname = _op_name(op)
+    init_v = _NEUTRAL[opname] if init is None else float(init)
+    _lib.check(_lib.lib().mk_accumulate_f32(dst.pointer(), src.pointer(), src.length, _lib.MK_OP[opname], init_v,
+                                            0 if inclusive else 1, current_stream_handle()), "accumulate!")
+    return dst
+
+
+def cumsum(src: MLIRArray) -> MLIRArray:
+    """``cumsum(x)`` / ``AK.cumsum(x)``: a new MLIRArray of running sums."""
+    from .array import MLIRCUDABackend, allocate
+    dst = allocate(MLIRCUDABackend(), "Float32", src.dims)
+    return accumulate(operator.add, dst, src)

@@ -111,6 +111,27 @@ MK_API int mk_mapreduce_f32_noalloc(double* out_dev, const float* x, int64_t n,
 /* sum(x.^2) == mk_mapreduce_f32(out, x, n, MK_F_ABS2, MK_OP_ADD, 0.0, stream). */
 MK_API int mk_sum_sq_f32(double* out_dev, const float* x, int64_t n, void* stream);
 
+/* Reduction of one dimension of a column-major Float32 array viewed as
+ * (pre, len, post), the reduced dimension in the middle:
+ *   out[p + q*pre] = op(init, op_{k<len} f(x[p + k*pre + q*pre*len]))
+ * for p < pre, q < post; out has pre*post Float32 elements (len == 0 gives
+ * init).  fp64 accumulation, one rounding to Float32; deterministic.  May use
+ * a per-stream workspace of up to 1024*pre*post doubles when pre*post is small.
+ * Replaces the dims form of GPUArrays.mapreducedim! (ext/MLIRCUDAExt.jl:114-119;
+ * sum/maximum/minimum(m; dims=d), test/test_gpuarrays.jl:98-107). */
+MK_API int mk_mapreduce_dim_f32(float* out, const float* x, int64_t pre, int64_t len, int64_t post,
+                                int f, int op, double init, void* stream);
+
+/* Prefix scan: out[i] = op(init, x[0], ..., x[i]) (inclusive) or
+ * op(init, x[0], ..., x[i-1]) (exclusive != 0; out[0] = init), op in
+ * {MK_OP_ADD, MK_OP_MAX, MK_OP_MIN, MK_OP_MUL}.  Single-pass decoupled
+ * look-back, fp64 carries, each output rounded once to Float32; bounded waits
+ * (MK_ERR_TIMEOUT via mk_error_poll).  Uses a per-stream workspace of about
+ * 5 bytes per 1024 elements.  out may alias x.  Replaces AK.accumulate! /
+ * cumsum on an MLIRArray (test/test_downstream_ka.jl:39-42, 75-78). */
+MK_API int mk_accumulate_f32(float* out, const float* x, int64_t n, int op, double init, int exclusive,
+                             void* stream);
+
 /* c[i] = a[idx1[i] - 1], i in [0, n); idx1 is 1-based into a[0, na).
  * Out-of-range indices write 0 and set the device error word.  Bit-exact.
  * Replaces a KA launch of `c[i] = a[idx[i]]` (indexing semantics

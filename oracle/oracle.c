@@ -114,6 +114,39 @@ double or_mapreduce_f64(const float* x, int64_t n, int f, int op, double init) {
   return acc;
 }
 
+/* dims reduction: out[p + q*pre] = op(init, op_k f(x[p + k*pre + q*pre*len]))
+ * in fp64 (the dims form of mapreducedim!, ext/MLIRCUDAExt.jl:114-119). */
+void or_mapreduce_dim_f64(double* out, const float* x, int64_t pre, int64_t len, int64_t post, int f, int op,
+                          double init) {
+  for (int64_t q = 0; q < post; ++q)
+    for (int64_t p = 0; p < pre; ++p) {
+      double acc = init;
+      for (int64_t k = 0; k < len; ++k) {
+        double v = map_f(f, x[p + k * pre + q * pre * len]);
+        if (op == OP_ADD) acc += v;
+        else if (op == OP_MUL) acc *= v;
+        else if (op == OP_MAX) acc = jl_max(acc, v);
+        else acc = jl_min(acc, v);
+      }
+      out[p + q * pre] = acc;
+    }
+}
+
+/* prefix scan in fp64 (AK.accumulate!/cumsum semantics, inclusive or
+ * exclusive with init first; test/test_downstream_ka.jl:39-42, 75-78). */
+void or_accumulate_f64(double* out, const float* x, int64_t n, int op, double init, int exclusive) {
+  double acc = init;
+  for (int64_t i = 0; i < n; ++i) {
+    if (exclusive) out[i] = acc;
+    double v = (double)x[i];
+    if (op == OP_ADD) acc += v;
+    else if (op == OP_MUL) acc *= v;
+    else if (op == OP_MAX) acc = jl_max(acc, v);
+    else acc = jl_min(acc, v);
+    if (!exclusive) out[i] = acc;
+  }
+}
+
 /* gather: c[i] = a[idx[i]], 1-based (src/lower.jl:4064-4077).  An index out of
  * [1, na] writes 0 and reports OR_ERR_DEVICE_FAULT (the reference raises a
  * BoundsError/KernelException without @inbounds). */

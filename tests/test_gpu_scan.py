@@ -1,0 +1,79 @@
+"""Prefix scan (mk_accumulate_f32) against the fp64 oracle: AK.accumulate! and
+cumsum (test/test_downstream_ka.jl:39-42 inclusive of 1:n, :75-78 exclusive).
+Bar: each output within 1e-6 of the running sum of |x| (one Float32 rounding
+of an fp64 carry); max/min exact."""
+import operator
+
+import numpy as np
+import pytest
+import torch
+
+import cutilecpu_b200 as mk
+import oracle
+from cutilecpu_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def scan(x: np.ndarray, op="add", init=0.0, exclusive=False, off=0, inplace=False) -> np.ndarray:
+    xd = torch.from_numpy(np.concatenate([np.zeros(off, np.float32), x])).cuda()
+    out = xd if inplace else torch.full_like(xd, np.nan)
+    rc = _lib.lib().mk_accumulate_f32(out.data_ptr() + 4 * off, xd.data_ptr() + 4 * off, x.size, _lib.MK_OP[op],
+                                      float(init), int(exclusive), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, _lib.last_error()
+    assert _lib.lib().mk_error_poll(torch.cuda.current_stream().cuda_stream) == 0
+    return out.cpu().numpy()[off:]
+
+
+def check_add(got, x, init=0.0, exclusive=False):
+    want = oracle.accumulate(x, "add", init, exclusive)
+    scale = np.abs(init) + np.cumsum(np.abs(x.astype(np.float64)))
+    assert np.all(np.abs(got - want) <= 1e-6 * scale + 1e-30)
+
+
+def test_cumsum_1_to_1024(cuda):
+    x = np.arange(1, 1025, dtype=np.float32)
+    np.testing.assert_array_equal(scan(x), np.cumsum(np.arange(1, 1025)).astype(np.float32))
+
+
+@pytest.mark.parametrize("n", [1, 2, 31, 4095, 4096, 4097, 100_000, (1 << 22) + 7, 1 << 26])
+@pytest.mark.parametrize("exclusive", [False, True])
+def test_scan_add_sizes(cuda, n, exclusive):
+    r = np.random.Generator(np.random.Philox(n))
+    x = (r.random(n, dtype=np.float32) * 2 - 1).astype(np.float32)
+    check_add(scan(x, exclusive=exclusive, init=0.5), x, 0.5, exclusive)
+
+
+@pytest.mark.parametrize("op,init", [("max", -np.inf), ("min", np.inf)])
+def test_scan_max_min_exact(cuda, op, init):
+    r = np.random.Generator(np.random.Philox(7))
+    x = r.standard_normal(300_001, dtype=np.float32)
+    np.testing.assert_array_equal(scan(x, op, init), oracle.accumulate(x, op, init).astype(np.float32))
+
+
+def test_scan_misaligned_and_inplace(cuda):
+    r = np.random.Generator(np.random.Philox(8))
+    x = r.random(50_001, dtype=np.float32)
+    check_add(scan(x, off=3), x)
+    check_add(scan(x, inplace=True), x)
+
+
+def test_scan_deterministic_property_full_size(cuda):
+    # size-independent property: the last inclusive value equals the sum
+    r = np.random.Generator(np.random.Philox(9))
+    n = 1 << 28
+    x = r.random(n, dtype=np.float32)
+    got = scan(x)
+    assert abs(float(got[-1]) - oracle.mapreduce(x)) <= 1e-6 * oracle.mapreduce(x)
+    assert np.all(np.diff(got[::4096]) >= 0)  # non-negative inputs: non-decreasing
+
+
+def test_surface_accumulate_and_cumsum(cuda):
+    src = mk.MLIRArray(np.arange(1, 1025, dtype=np.float32))
+    dst = mk.zeros(mk.get_backend(src), "Float32", 1024)
+    mk.accumulate(operator.add, dst, src, init=0.0)
+    np.testing.assert_array_equal(mk.Array(dst), np.cumsum(np.arange(1, 1025)).astype(np.float32))
+    np.testing.assert_array_equal(mk.Array(mk.cumsum(src)), mk.Array(dst))
+    ex = mk.zeros(mk.get_backend(src), "Float32", 1024)
+    mk.accumulate(operator.add, ex, src, init=0.0, inclusive=False)
+    np.testing.assert_array_equal(mk.Array(ex)[1:], mk.Array(dst)[:-1])
