@@ -8,7 +8,7 @@ computation runs in ``libkernels.so`` (C ABI: include/mk_kernels.h).
 from ._lib import KernelException, MLIRKernelsError
 from .array import (Array, MLIRArray, MLIRCUDABackend, allocate, copyto, functional, get_backend,
                     launch_config, ones, supports_atomics, synchronize, zeros)
-from .kernels import Kernel, KernelFunction, gather, histogram, mm_tiled, mm_tiled_simt, vadd
+from .kernels import Kernel, KernelFunction, gather, histogram, mm_naive, mm_tiled, mm_tiled_simt, mul, vadd
 from .reductions import (Broadcasted, abs2, accumulate, cumsum, count, identity, mapreduce, mapreducedim, maximum, minimum,
                      positive, prod, reduce, sum)
 from . import distributed, reductions
@@ -16,7 +16,7 @@ from . import distributed, reductions
 __all__ = [
     "KernelException", "MLIRKernelsError", "Array", "MLIRArray", "MLIRCUDABackend", "allocate",
     "copyto", "functional", "get_backend", "launch_config", "ones", "supports_atomics", "synchronize",
-    "zeros", "Kernel", "KernelFunction", "gather", "histogram", "mm_tiled", "mm_tiled_simt", "vadd", "Broadcasted",
+    "zeros", "Kernel", "KernelFunction", "gather", "histogram", "mm_naive", "mm_tiled", "mm_tiled_simt", "mul", "vadd", "Broadcasted",
     "abs2", "accumulate", "cumsum", "count", "identity", "mapreduce", "mapreducedim", "maximum", "minimum", "positive", "prod",
     "reduce", "sum", "distributed",
 ]

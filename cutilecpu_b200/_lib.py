@@ -37,6 +37,7 @@ SIGNATURES = {
     "mk_gather_f32": (_int, [_vp, _vp, _i64, _vp, _i64, _vp]),
     "mk_hist_u32": (_int, [_vp, _i32, _vp, _i64, _vp]),
     "mk_sgemm_3xtf32": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "mk_sgemm_f32": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "mk_matmul_tiled16_f32": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
 }
 

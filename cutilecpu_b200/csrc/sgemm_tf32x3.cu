@@ -39,6 +39,7 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <string>
 
 #include "mk_common.cuh"
 
@@ -176,7 +177,7 @@ __device__ __forceinline__ float4 segment_part(float4 x, int i) {
 constexpr int SA_ROWS = 128;
 constexpr int SA_KBS = 2;
 __global__ void __launch_bounds__(256) split_a(float* __restrict__ A2, const float* __restrict__ A, int64_t M,
-                                               int64_t lda, int nkb) {
+                                               int64_t lda, int nkb, int64_t kvalid) {
   __shared__ float t[SA_KBS * KB][SA_ROWS + 1];
   const int64_t m0 = (int64_t)blockIdx.x * SA_ROWS;
   const int kb0 = blockIdx.y * SA_KBS;
@@ -184,7 +185,8 @@ __global__ void __launch_bounds__(256) split_a(float* __restrict__ A2, const flo
   for (int e = threadIdx.x; e < SA_KBS * KB * SA_ROWS; e += 256) {
     const int kk = e / SA_ROWS, mm = e % SA_ROWS;
     const int64_t m = m0 + mm;
-    t[kk][mm] = (kk < nk && m < M) ? A[m + (int64_t)(kb0 * KB + kk) * lda] : 0.0f;
+    const int64_t k = (int64_t)kb0 * KB + kk;  // columns at or past kvalid are zero padding
+    t[kk][mm] = (kk < nk && m < M && k < kvalid) ? A[m + k * lda] : 0.0f;
   }
   __syncthreads();
   const int64_t row_len = (int64_t)nkb * ROWF;
@@ -207,7 +209,7 @@ __global__ void __launch_bounds__(256) split_a(float* __restrict__ A2, const flo
 // allow 16-byte loads.
 template <bool VEC>
 __global__ void __launch_bounds__(256) split_b(float* __restrict__ B2, const float* __restrict__ B, int64_t N,
-                                               int64_t ldb, int nkb) {
+                                               int64_t ldb, int nkb, int64_t kvalid) {
   const int64_t total = N * (int64_t)nkb * 8;  // float4 outputs
   const int64_t stride = (int64_t)gridDim.x * 256;
   for (int64_t t = (int64_t)blockIdx.x * 256 + threadIdx.x; t < total; t += stride) {
@@ -215,8 +217,15 @@ __global__ void __launch_bounds__(256) split_b(float* __restrict__ B2, const flo
     const int i = (int)(t & 7);
     const int64_t n = seg / nkb;
     const int kb = (int)(seg - n * nkb);
-    const float* src = B + n * ldb + (int64_t)kb * KB + 4 * (i & 3);
-    const float4 x = VEC ? *reinterpret_cast<const float4*>(src) : make_float4(src[0], src[1], src[2], src[3]);
+    const int64_t k = (int64_t)kb * KB + 4 * (i & 3);
+    const float* src = B + n * ldb + k;
+    float4 x;
+    if (VEC && k + 4 <= kvalid) {
+      x = *reinterpret_cast<const float4*>(src);
+    } else {  // unaligned B, or the zero-padded K remainder
+      x = make_float4(k < kvalid ? src[0] : 0.0f, k + 1 < kvalid ? src[1] : 0.0f, k + 2 < kvalid ? src[2] : 0.0f,
+                      k + 3 < kvalid ? src[3] : 0.0f);
+    }
     reinterpret_cast<float4*>(B2)[t] = segment_part(x, i);
   }
 }
@@ -446,21 +455,28 @@ cudaError_t g_attr_err = cudaSuccess;
 
 }  // namespace
 
-extern "C" int mk_sgemm_3xtf32(float* C, const float* A, const float* B, int64_t M, int64_t N, int64_t K,
-                               int64_t lda, int64_t ldb, int64_t ldc, void* stream) {
-  MK_ENTRY_DEVICE(dev);
-  if (M < 0 || N < 0 || K < 0) return mk::fail(MK_ERR_INVALID, "mk_sgemm_3xtf32: negative size");
+namespace {
+
+// full_k: every K term (LinearAlgebra.mul!); otherwise 16*floor(K/16) terms
+// (mm_tiled!).  The remainder of a full-K product is zero-padded by the split.
+int sgemm_impl(const char* name, bool full_k, float* C, const float* A, const float* B, int64_t M, int64_t N,
+               int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void* stream) {
+  mk::Device* dev = mk::current_device();
+  if (!dev) return MK_ERR_CUDA;
+  const std::string who(name);
+  if (M < 0 || N < 0 || K < 0) return mk::fail(MK_ERR_INVALID, who + ": negative size");
   if (M == 0 || N == 0) return MK_OK;
   if (lda < M || ldb < K || ldc < M || lda < 1 || ldb < 1)
-    return mk::fail(MK_ERR_INVALID, "mk_sgemm_3xtf32: leading dimension too small");
-  const int64_t Kt = (K / KB) * KB;
-  if (!C || (Kt > 0 && (!A || !B))) return mk::fail(MK_ERR_INVALID, "mk_sgemm_3xtf32: null pointer");
+    return mk::fail(MK_ERR_INVALID, who + ": leading dimension too small");
+  const int64_t Kt = full_k ? mk::cdiv(K, KB) * KB : (K / KB) * KB;  // padded / truncated K
+  const int64_t kvalid = full_k ? K : Kt;
+  if (!C || (Kt > 0 && (!A || !B))) return mk::fail(MK_ERR_INVALID, who + ": null pointer");
   if (mk::cdiv(M, BM) * mk::cdiv(N, BN) > INT32_MAX || M > INT32_MAX || N > INT32_MAX || mk::cdiv(Kt / KB, SA_KBS) > 65535)
-    return mk::fail(MK_ERR_INVALID, "mk_sgemm_3xtf32: problem too large");
+    return mk::fail(MK_ERR_INVALID, who + ": problem too large");
   cudaStream_t s = mk::as_stream(stream);
   if (Kt == 0) {
     cudaError_t e = cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)M * 4, (size_t)N, s);
-    return e == cudaSuccess ? MK_OK : mk::fail_cuda(e, "mk_sgemm_3xtf32: zero fill");
+    return e == cudaSuccess ? MK_OK : mk::fail_cuda(e, "sgemm: zero fill");
   }
   const int nkb = (int)(Kt / KB);
   const uint64_t cols = (uint64_t)nkb * ROWF;
@@ -472,16 +488,16 @@ extern "C" int mk_sgemm_3xtf32(float* C, const float* A, const float* B, int64_t
   float* A2 = static_cast<float*>(ws);
   float* B2 = reinterpret_cast<float*>(static_cast<char*>(ws) + a_bytes);
 
-  split_a<<<dim3((unsigned)mk::cdiv(M, SA_ROWS), (unsigned)mk::cdiv(nkb, SA_KBS)), 256, 0, s>>>(A2, A, M, lda, nkb);
+  split_a<<<dim3((unsigned)mk::cdiv(M, SA_ROWS), (unsigned)mk::cdiv(nkb, SA_KBS)), 256, 0, s>>>(A2, A, M, lda, nkb, kvalid);
   {
     const int64_t total = N * (int64_t)nkb * 8;
     int64_t blocks = mk::cdiv(total, 256);
     const int64_t cap = (int64_t)dev->sms * 8;
     if (blocks > cap) blocks = cap;
     if (mk::aligned16(B) && ldb % 4 == 0)
-      split_b<true><<<(unsigned)blocks, 256, 0, s>>>(B2, B, N, ldb, nkb);
+      split_b<true><<<(unsigned)blocks, 256, 0, s>>>(B2, B, N, ldb, nkb, kvalid);
     else
-      split_b<false><<<(unsigned)blocks, 256, 0, s>>>(B2, B, N, ldb, nkb);
+      split_b<false><<<(unsigned)blocks, 256, 0, s>>>(B2, B, N, ldb, nkb, kvalid);
   }
   CUtensorMap mapA, mapB;
   if ((rc = make_map(&mapA, A2, cols, (uint64_t)M, BM)) != MK_OK) return rc;
@@ -495,4 +511,18 @@ extern "C" int mk_sgemm_3xtf32(float* C, const float* A, const float* B, int64_t
   sgemm_tf32x3<<<grid, kThreads, SMEM_BYTES, s>>>(mapA, mapB, C, M, N, ldc, nkb, mk::wait_limit_cycles(),
                                                    dev->err_word);
   return mk::check_launch("mk_sgemm_3xtf32: launch");
+}
+
+}  // namespace
+
+extern "C" int mk_sgemm_3xtf32(float* C, const float* A, const float* B, int64_t M, int64_t N, int64_t K,
+                               int64_t lda, int64_t ldb, int64_t ldc, void* stream) {
+  mk::clear_error();
+  return sgemm_impl("mk_sgemm_3xtf32", false, C, A, B, M, N, K, lda, ldb, ldc, stream);
+}
+
+extern "C" int mk_sgemm_f32(float* C, const float* A, const float* B, int64_t M, int64_t N, int64_t K,
+                            int64_t lda, int64_t ldb, int64_t ldc, void* stream) {
+  mk::clear_error();
+  return sgemm_impl("mk_sgemm_f32", true, C, A, B, M, N, K, lda, ldb, ldc, stream);
 }

@@ -16,6 +16,7 @@ kernel             reference definition                        C entry point
 ``gather``         ``c[i] = a[idx[i]]`` (src/lower.jl:4031)    mk_gather_f32
 ``histogram``      test/test_ka_cpu.jl:16-19, test_gpu_simt:49  mk_hist_u32
 ``mm_tiled``       examples/tiled_matmul.jl:28-48              mk_sgemm_3xtf32
+``mm_naive``       examples/tiled_matmul.jl:12-19              mk_sgemm_f32
 ``mm_tiled_simt``  examples/tiled_matmul.jl:28-48 (SIMT)       mk_matmul_tiled16_f32
 =================  =========================================  ===========================
 
@@ -182,6 +183,20 @@ def _launch_mm_tiled(args, nd, wg, stream) -> None:
         "mm_tiled!")
 
 
+def _launch_mm_naive(args, nd, wg, stream) -> None:
+    Cm, A, B, M, N, K = _matmul_operands(args, nd, "mm_naive!")
+    _lib.check(_lib.lib().mk_sgemm_f32(
+        Cm.pointer(), A.pointer(), B.pointer(), M, N, K, A.size(1), B.size(1), Cm.size(1), stream),
+        "mm_naive!")
+
+
+def mul(Cm: MLIRArray, A: MLIRArray, B: MLIRArray) -> MLIRArray:
+    """``LinearAlgebra.mul!(C, A, B)`` on MLIRArrays: C = A*B over all K terms
+    on the tcgen05 tensor cores (3xTF32)."""
+    _launch_mm_naive((Cm, A, B), (A.size(1), B.size(2)), None, current_stream_handle())
+    return Cm
+
+
 def _launch_mm_tiled_simt(args, nd, wg, stream) -> None:
     Cm, A, B, M, N, K = _matmul_operands(args, nd, "mm_tiled!")
     _lib.check(_lib.lib().mk_matmul_tiled16_f32(
@@ -192,6 +207,8 @@ def _launch_mm_tiled_simt(args, nd, wg, stream) -> None:
 vadd = KernelFunction("vadd!", 1, _launch_vadd)
 gather = KernelFunction("gather!", 1, _launch_gather)
 histogram = KernelFunction("histogram!", 1, _launch_histogram)
+# mm_naive! (one output per thread, all K terms; examples/tiled_matmul.jl:12-19).
+mm_naive = KernelFunction("mm_naive!", 2, _launch_mm_naive)
 # mm_tiled! on the tcgen05 tensor cores in 3xTF32 (the hot path).
 mm_tiled = KernelFunction("mm_tiled!", 2, _launch_mm_tiled, static_wg=(16, 16))
 # The reference's 16x16 @localmem kernel run on CUDA cores (SIMT comparison point).

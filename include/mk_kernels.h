@@ -161,6 +161,15 @@ MK_API int mk_sgemm_3xtf32(float* C, const float* A, const float* B,
                            int64_t M, int64_t N, int64_t K,
                            int64_t lda, int64_t ldb, int64_t ldc, void* stream);
 
+/* LinearAlgebra.mul!(C, A, B) on MLIRArrays: the same tcgen05 3xTF32 GEMM as
+ * mk_sgemm_3xtf32 but over ALL K terms (the K % 16 remainder is zero-padded in
+ * the split operands), i.e. the semantics of the naive kernel mm_naive!
+ * (examples/tiled_matmul.jl:12-19, which the reference benchmarks against
+ * CUBLAS mul! at :85).  Same layout, workspace and accuracy. */
+MK_API int mk_sgemm_f32(float* C, const float* A, const float* B,
+                        int64_t M, int64_t N, int64_t K,
+                        int64_t lda, int64_t ldb, int64_t ldc, void* stream);
+
 /* The reference's own algorithm on CUDA cores: one output per thread, 16x16
  * shared-memory tiles, K % 16 ignored (examples/tiled_matmul.jl:28-48).  Kept
  * as the SIMT comparison point for the tensor-core path; same argument rules. */

@@ -107,3 +107,38 @@ def test_sgemm_full_size_properties(cuda):
     assert np.linalg.norm(got - want) / np.linalg.norm(want) <= RTOL_FRO
     ii = np.array([0, 1, 127, 128, 4095, 8191, 8191]); jj = np.array([0, 255, 256, 17, 4000, 0, 8191])
     np.testing.assert_allclose(C[ii, jj], oracle.matmul_entries_f64(A, B, ii, jj), rtol=1e-4, atol=2e-4)
+
+
+def sgemm_full(A_h, B_h):
+    M, K = A_h.shape
+    N = B_h.shape[1]
+    A, B = dev(A_h), dev(B_h)
+    Cd = torch.empty(M * N, device="cuda")
+    rc = _lib.lib().mk_sgemm_f32(Cd.data_ptr(), A.data_ptr(), B.data_ptr(), M, N, K, M, K, M,
+                                 torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, _lib.last_error()
+    return Cd.cpu().numpy().reshape((M, N), order="F")
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 32, 1), (100, 70, 15), (129, 257, 17), (256, 256, 33), (300, 200, 1000)])
+def test_sgemm_full_k_vs_fp64(cuda, M, N, K):
+    r = np.random.Generator(np.random.Philox(M + N + K))
+    A = np.asfortranarray(r.standard_normal((M, K), dtype=np.float32))
+    B = np.asfortranarray(r.standard_normal((K, N), dtype=np.float32))
+    want = A.astype(np.float64) @ B.astype(np.float64)
+    assert frob_rel(sgemm_full(A, B), want) <= RTOL_FRO
+
+
+def test_mul_and_mm_naive_surface(cuda):
+    import cutilecpu_b200 as mk
+    r = np.random.Generator(np.random.Philox(5))
+    A = np.asfortranarray(r.standard_normal((8, 4), dtype=np.float32))
+    B = np.asfortranarray(r.standard_normal((4, 6), dtype=np.float32))
+    Am, Bm = mk.MLIRArray(A), mk.MLIRArray(B)
+    Cm = mk.zeros(mk.get_backend(Am), "Float32", (8, 6))
+    mk.mul(Cm, Am, Bm)
+    want = A.astype(np.float64) @ B.astype(np.float64)
+    assert np.max(np.abs(mk.Array(Cm) - want)) < 1e-5      # test/test_gpu_simt.jl:335 uses < 1f-3
+    C2 = mk.zeros(mk.get_backend(Am), "Float32", (8, 6))
+    mk.mm_naive(mk.get_backend(Am), (4, 2))(C2, Am, Bm, ndrange=(8, 6))
+    np.testing.assert_array_equal(mk.Array(C2), mk.Array(Cm))
