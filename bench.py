@@ -301,6 +301,98 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
                                                self.idx_host.ctypes.data, self.n, 256), \
                 self.units_per_step, "full 2^27 gather, W=256"
 
+    class Scan(Workload):
+        name = "scan"
+        metric = "accumulate!(+) / cumsum HBM GB/s (8 B/element)"
+        cfg = {"n": 1 << 28}
+
+        def __init__(self):
+            super().__init__(rank, world)
+            n = self.n = n_override or self.cfg["n"]
+            self.x_host = workloads.uniform01(n, stream=50 + 100 * rank)
+            self.x = mk.MLIRArray(self.x_host)
+            self.y = mk.zeros(be, "Float32", n)
+            self.units_per_step = 8.0 * n
+            self.h2d_bytes, self.d2h_bytes = 4 * n, 4 * n
+            self.config = {"workload": "cumsum of Float32 x ~ U[0,1), n=2^28 per GPU (scope row f2: AK.accumulate!)",
+                           "n_per_gpu": n, "l2": "input (1 GiB) larger than L2; no flush"}
+
+        def launch(self):
+            _lib.check(L.mk_accumulate_f32(self.y.pointer(), self.x.pointer(), self.n, 0, 0.0, 0, stream()), "scan")
+
+        def combine(self):
+            pass
+
+        def check(self):
+            got = float(self.y.storage[-1].item())
+            want = float(np.sum(self.x_host, dtype=np.float64))
+            assert abs(got - want) <= 1e-6 * want, (got, want)
+
+        def e2e_setup(self):
+            self.px = torch.from_numpy(self.x_host).pin_memory()
+            self.py = torch.empty(self.n, dtype=torch.float32).pin_memory()
+
+        def e2e_step(self):
+            mk.copyto(be, self.x, self.px)
+            mk.accumulate(operator.add, self.y, self.x)
+            mk.copyto(be, self.py, self.y)
+            torch.cuda.current_stream().synchronize()
+
+        def cpu_sample(self, threads):
+            import oracle
+            Lo = oracle.lib()
+            out = np.empty(self.n, dtype=np.float32)
+            tot = np.empty(self.n // 512 + 2, dtype=np.float32)
+            return lambda: Lo.mlirb_cumsum_f32(out.ctypes.data, self.x_host.ctypes.data, self.n, 256, tot.ctypes.data), \
+                self.units_per_step, "full 2^28 cumsum: per-block fp32 scans + block-prefix pass, W=256"
+
+    class Dims(Workload):
+        name = "reduce_dims"
+        metric = "sum(m; dims=1) HBM GB/s (4 B/element)"
+        cfg = {"n": 1 << 14}
+
+        def __init__(self):
+            super().__init__(rank, world)
+            r = self.r = n_override or self.cfg["n"]
+            self.c = r
+            self.m_host = workloads.uniform01(r * r, stream=60 + 100 * rank)
+            self.m = mk.MLIRArray(self.m_host.reshape((r, r), order="F"))
+            self.out = mk.zeros(be, "Float32", (1, r))
+            self.units_per_step = 4.0 * r * r
+            self.h2d_bytes, self.d2h_bytes = 4 * r * r, 4 * r
+            self.config = {"workload": "sum(m; dims=1) of a 16384x16384 Float32 matrix per GPU "
+                                       "(scope row f1: dims reductions)", "rows": r, "cols": r,
+                           "l2": "input (1 GiB) larger than L2; no flush"}
+
+        def launch(self):
+            _lib.check(L.mk_mapreduce_dim_f32(self.out.pointer(), self.m.pointer(), 1, self.r, self.c, 0, 0, 0.0,
+                                              stream()), "dims")
+
+        def combine(self):
+            pass
+
+        def check(self):
+            got = mk.Array(self.out).ravel()[:8]
+            want = self.m_host.reshape((self.r, self.c), order="F")[:, :8].astype(np.float64).sum(0)
+            np.testing.assert_allclose(got, want, rtol=1e-5)
+
+        def e2e_setup(self):
+            self.pm = torch.from_numpy(self.m_host).pin_memory()
+            self.po = torch.empty(self.c, dtype=torch.float32).pin_memory()
+
+        def e2e_step(self):
+            mk.copyto(be, self.m, self.pm)
+            mk.reductions.mapreduce_dims_into(mk.identity, operator.add, self.out, self.m, 1)
+            mk.copyto(be, self.po, self.out)
+            torch.cuda.current_stream().synchronize()
+
+        def cpu_sample(self, threads):
+            import oracle
+            Lo = oracle.lib()
+            out = np.empty(self.c, dtype=np.float32)
+            return lambda: Lo.mlirb_sum_dims1_f32(out.ctypes.data, self.m_host.ctypes.data, self.r, self.c), \
+                self.units_per_step, "full 16384x16384 sum(m; dims=1), OpenMP over columns"
+
     class Histogram(Workload):
         name = "histogram"
         metric = "histogram HBM GB/s (4 B/key)"
@@ -464,7 +556,8 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
                 2.0 * self.m * cols * self.k, f"C[:, 1:{cols}] of the 8192^3 product (restated 16x16 tiles)"
 
     table = {"reduce": Reduce, "vadd": Vadd, "gather": Gather, "histogram": Histogram,
-             "matmul": Matmul, "matmul_simt": MatmulSimt}
+             "matmul": Matmul, "matmul_simt": MatmulSimt,
+             "scan": Scan, "reduce_dims": Dims}
     return table[kind]()
 
 
@@ -663,6 +756,21 @@ def run_reference(kind: str, args, world: int = 1) -> dict:
         units, unit, metric = 4.0 * m, "GB/s", "histogram HBM GB/s (4 B/key)"
         sample = "first 2^24 of the 2^26 Zipf keys per step"
         conf = "histogram Int32 keys ~ Zipf(1.1) on 1..4096 (configs[3])"
+    elif kind == "scan":
+        n = 1 << 28
+        x = workloads.uniform01(n, stream=50)
+        out = np.empty(n, dtype=np.float32)
+        tot = np.empty(n // 512 + 2, dtype=np.float32)
+        fn = lambda: L.mlirb_cumsum_f32(out.ctypes.data, x.ctypes.data, n, 256, tot.ctypes.data)  # noqa: E731
+        units, unit, metric = 8.0 * n, "GB/s", "accumulate!(+) / cumsum HBM GB/s (8 B/element)"
+        sample, conf = "full 2^28 cumsum per step", "cumsum Float32 n=2^28"
+    elif kind == "reduce_dims":
+        r = 1 << 14
+        m = workloads.uniform01(r * r, stream=60)
+        out = np.empty(r, dtype=np.float32)
+        fn = lambda: L.mlirb_sum_dims1_f32(out.ctypes.data, m.ctypes.data, r, r)  # noqa: E731
+        units, unit, metric = 4.0 * r * r, "GB/s", "sum(m; dims=1) HBM GB/s (4 B/element)"
+        sample, conf = "full 16384x16384 sum(m; dims=1) per step", "sum(m; dims=1) Float32 16384x16384"
     else:
         m = cfg["matmul"]["m"]
         A = workloads.normal((m, m), stream=40)
@@ -699,14 +807,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--kernel", default="reduce",
-                    choices=["reduce", "vadd", "gather", "histogram", "matmul", "matmul_simt", "all"])
+                    choices=["reduce", "vadd", "gather", "histogram", "matmul", "matmul_simt", "scan", "reduce_dims",
+                             "all"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--n", type=int, default=None,
                     help="override the element count of the configuration (small profiling cases)")
     args = ap.parse_args()
-    kinds = ["reduce", "vadd", "gather", "histogram", "matmul", "matmul_simt"] if args.kernel == "all" else [args.kernel]
+    kinds = (["reduce", "vadd", "gather", "histogram", "matmul", "matmul_simt", "scan", "reduce_dims"]
+             if args.kernel == "all" else [args.kernel])
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -729,7 +839,7 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     defaults = {"reduce": (2000, 50), "vadd": (2000, 50), "gather": (200, 10), "histogram": (500, 20),
-                "matmul": (20, 3), "matmul_simt": (3, 1)}
+                "matmul": (20, 3), "matmul_simt": (3, 1), "scan": (500, 20), "reduce_dims": (1000, 20)}
     try:
         for k in kinds:
             a = argparse.Namespace(**vars(args))

@@ -136,6 +136,21 @@ int stream_workspace(Device* d, cudaStream_t s, size_t bytes, void** out, int sl
   return MK_OK;
 }
 
+int allow_dynamic_smem(const void* kernel, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, size_t> done;
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lk(mu);
+  size_t& have = done[std::make_pair(dev, kernel)];
+  if (have >= bytes) return MK_OK;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+  have = bytes;
+  return MK_OK;
+}
+
 unsigned long long wait_limit_cycles() {
   static unsigned long long v = [] {
     const char* e = getenv("MK_WAIT_LIMIT_CYCLES");

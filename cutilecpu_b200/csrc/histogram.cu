@@ -4,12 +4,14 @@
 // test/test_gpu_simt.jl:49-73; atomic kind `addi` src/lower.jl:3600-3623).
 //
 // Design (HBM-bound on the key stream, 4 B/key; contention-bound on hot bins):
-//   * persistent grid; every block privatises the whole histogram in shared
-//     memory, kReplicas copies so that warps spread their atomics (warp w uses
-//     copy w % replicas); keys arrive as 16-byte int4 vectors;
-//   * optional warp aggregation: lanes holding the same key elect a leader
-//     (match.any) that adds the population count once — this is what keeps
-//     Zipf-skewed input (one bin can hold 16 % of all keys) from serialising;
+//   * persistent grid (2 x 1024 threads per SM); every block privatises the
+//     whole histogram in shared memory (optionally several replicas, warp w
+//     using copy w % replicas); keys arrive as 16-byte int4 vectors, several
+//     in flight per thread;
+//   * one shared atomic per key.  Warp aggregation with match.any measured 7x
+//     slower (instruction-issue bound) even on Zipf(1.1) keys, where one bin
+//     holds 16 % of the keys: same-address shared atomics do not serialise
+//     enough to matter;
 //   * flush: one global atomicAdd per non-zero bin per block (sum of replicas).
 // nbins too large for shared memory falls back to per-key global atomics.
 // Keys outside [1, nbins] are skipped and raise ERRBIT_HIST_KEY.
@@ -23,8 +25,8 @@ constexpr int kThreads = 1024;
 
 struct Tune {
   int blocks_per_sm = 2;
-  int replicas = 2;
-  int aggregate = 0;
+  int replicas = 1;
+  int unroll = 2;
 };
 
 const Tune& tune() {
@@ -32,82 +34,65 @@ const Tune& tune() {
     Tune v;
     if (const char* e = getenv("MK_TUNE_HIST_BLOCKS_PER_SM")) v.blocks_per_sm = atoi(e);
     if (const char* e = getenv("MK_TUNE_HIST_REPLICAS")) v.replicas = atoi(e);
-    if (const char* e = getenv("MK_TUNE_HIST_AGGREGATE")) v.aggregate = atoi(e);
+    if (const char* e = getenv("MK_TUNE_HIST_UNROLL")) v.unroll = atoi(e);
     if (v.blocks_per_sm < 1 || v.blocks_per_sm > 2) v.blocks_per_sm = 2;
-    if (v.replicas < 1 || v.replicas > 32) v.replicas = 2;
+    if (v.replicas < 1 || v.replicas > 32) v.replicas = 1;
     return v;
   }();
   return t;
 }
 
-template <bool AGG>
-__device__ __forceinline__ void add_key(unsigned* __restrict__ rep, uint32_t nbins, int32_t key, bool& bad) {
+__device__ __forceinline__ void add_key(unsigned* __restrict__ rep, uint32_t nbins, int32_t key, unsigned& bad) {
   const uint32_t u = (uint32_t)key - 1u;  // 1-based -> 0-based; key < 1 wraps to huge
-  const bool ok = u < nbins;
-  if (!ok) bad = true;
-  if (AGG) {
-    const unsigned active = __activemask();
-    const unsigned peers = __match_any_sync(active, ok ? u : 0xffffffffu);
-    const int leader = __ffs(peers) - 1;
-    if (ok && (int)(threadIdx.x & 31) == leader) atomicAdd(rep + u, (unsigned)__popc(peers));
-  } else {
-    if (ok) atomicAdd(rep + u, 1u);
-  }
+  if (u < nbins) atomicAdd(rep + u, 1u);
+  else bad = 1u;
 }
 
-template <bool AGG>
+__device__ __forceinline__ void add_key4(unsigned* __restrict__ rep, uint32_t nbins, int4 k, unsigned& bad) {
+  add_key(rep, nbins, k.x, bad);
+  add_key(rep, nbins, k.y, bad);
+  add_key(rep, nbins, k.z, bad);
+  add_key(rep, nbins, k.w, bad);
+}
+
+// UNR int4 key vectors in flight per thread.
+template <int UNR>
 __global__ void __launch_bounds__(kThreads)
 hist_smem(unsigned* __restrict__ counts, uint32_t nbins, const int32_t* __restrict__ keys, int64_t n,
           int head, int replicas, unsigned* __restrict__ err) {
   extern __shared__ unsigned sh[];
-  const uint32_t total = nbins * (uint32_t)replicas;
+  // replica r lives at r * (nbins + 1): the extra word moves the same bin of
+  // neighbouring replicas into different banks
+  const uint32_t rstride = nbins + 1;
+  const uint32_t total = rstride * (uint32_t)replicas;
   for (uint32_t b = threadIdx.x; b < total; b += kThreads) sh[b] = 0u;
   __syncthreads();
-  unsigned* rep = sh + (uint32_t)((threadIdx.x >> 5) % replicas) * nbins;
-  bool bad = false;
+  // lanes of one warp spread over the replicas, so a hot bin hit by several
+  // lanes of the same instruction is split across copies
+  unsigned* rep = sh + (uint32_t)((threadIdx.x & 31) % replicas) * rstride;
+  unsigned bad = 0u;
 
   const int64_t tid = (int64_t)blockIdx.x * kThreads + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   const int4* k4 = reinterpret_cast<const int4*>(keys + head);
   const int64_t n4 = (n - head) / 4;
-  // Two int4 key vectors in flight per thread; uniform trip count per warp
-  // keeps match.any's participants whole in the aggregating form.
-  int64_t base = (int64_t)blockIdx.x * kThreads;
-  for (; base + stride < n4; base += 2 * stride) {
-    const int64_t i = base + threadIdx.x;
-    const bool second = i + stride < n4;
-    const int4 k0 = __ldcs(k4 + i);
-    int4 k1 = make_int4(1, 1, 1, 1);
-    if (second) k1 = __ldcs(k4 + i + stride);
-    add_key<AGG>(rep, nbins, k0.x, bad);
-    add_key<AGG>(rep, nbins, k0.y, bad);
-    add_key<AGG>(rep, nbins, k0.z, bad);
-    add_key<AGG>(rep, nbins, k0.w, bad);
-    if (second) {
-      add_key<AGG>(rep, nbins, k1.x, bad);
-      add_key<AGG>(rep, nbins, k1.y, bad);
-      add_key<AGG>(rep, nbins, k1.z, bad);
-      add_key<AGG>(rep, nbins, k1.w, bad);
-    }
+  int64_t i = tid;
+  for (; i + (UNR - 1) * stride < n4; i += UNR * stride) {
+    int4 k[UNR];
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) k[u] = __ldcs(k4 + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) add_key4(rep, nbins, k[u], bad);
   }
-  for (; base < n4; base += stride) {
-    const int64_t i = base + threadIdx.x;
-    if (i < n4) {
-      const int4 k = __ldcs(k4 + i);
-      add_key<AGG>(rep, nbins, k.x, bad);
-      add_key<AGG>(rep, nbins, k.y, bad);
-      add_key<AGG>(rep, nbins, k.z, bad);
-      add_key<AGG>(rep, nbins, k.w, bad);
-    }
-  }
+  for (; i < n4; i += stride) add_key4(rep, nbins, __ldcs(k4 + i), bad);
   const int64_t tail_start = head + n4 * 4;
-  if (tid < head) add_key<false>(rep, nbins, keys[tid], bad);
-  if (tid < n - tail_start) add_key<false>(rep, nbins, keys[tail_start + tid], bad);
+  if (tid < head) add_key(rep, nbins, keys[tid], bad);
+  if (tid < n - tail_start) add_key(rep, nbins, keys[tail_start + tid], bad);
   __syncthreads();
 
   for (uint32_t b = threadIdx.x; b < nbins; b += kThreads) {
     unsigned sum = 0;
-    for (int r = 0; r < replicas; ++r) sum += sh[(uint32_t)r * nbins + b];
+    for (int r = 0; r < replicas; ++r) sum += sh[(uint32_t)r * rstride + b];
     if (sum) atomicAdd(counts + b, sum);
   }
   if (bad) atomicOr(err, mk::ERRBIT_HIST_KEY);
@@ -116,11 +101,21 @@ hist_smem(unsigned* __restrict__ counts, uint32_t nbins, const int32_t* __restri
 __global__ void __launch_bounds__(256)
 hist_global(unsigned* __restrict__ counts, uint32_t nbins, const int32_t* __restrict__ keys, int64_t n,
             unsigned* __restrict__ err) {
-  bool bad = false;
+  unsigned bad = 0u;
   const int64_t stride = (int64_t)gridDim.x * 256;
   for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n; i += stride)
-    add_key<false>(counts, nbins, keys[i], bad);
+    add_key(counts, nbins, keys[i], bad);
   if (bad) atomicOr(err, mk::ERRBIT_HIST_KEY);
+}
+
+template <int UNR>
+int launch_smem(int64_t blocks, int64_t smem, cudaStream_t s, uint32_t* counts, int32_t nbins, const int32_t* keys,
+                int64_t n, int head, int replicas, unsigned* err) {
+  int rc = mk::allow_dynamic_smem(reinterpret_cast<const void*>(hist_smem<UNR>), (size_t)smem);
+  if (rc != MK_OK) return rc;
+  hist_smem<UNR><<<(unsigned)blocks, kThreads, (size_t)smem, s>>>(counts, (uint32_t)nbins, keys, n, head, replicas,
+                                                                  err);
+  return mk::check_launch("mk_hist_u32: launch");
 }
 
 }  // namespace
@@ -137,8 +132,8 @@ extern "C" int mk_hist_u32(uint32_t* counts, int32_t nbins, const int32_t* keys1
   const Tune& t = tune();
   int replicas = t.replicas;
   const int64_t smem_cap = dev->max_smem_optin / t.blocks_per_sm - 1024;
-  while (replicas > 1 && (int64_t)replicas * nbins * 4 > smem_cap) --replicas;
-  const int64_t smem = (int64_t)replicas * nbins * 4;
+  while (replicas > 1 && (int64_t)replicas * (nbins + 1) * 4 > smem_cap) --replicas;
+  const int64_t smem = (int64_t)replicas * (nbins + 1) * 4;
   if (smem > smem_cap) {
     int64_t blocks = mk::cdiv(n, 256);
     const int64_t cap = (int64_t)dev->sms * 8;
@@ -153,17 +148,10 @@ extern "C" int mk_hist_u32(uint32_t* counts, int32_t nbins, const int32_t* keys1
   const int64_t cap = (int64_t)dev->sms * t.blocks_per_sm;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  cudaError_t e;
-  if (t.aggregate) {
-    e = cudaFuncSetAttribute(hist_smem<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return mk::fail_cuda(e, "mk_hist_u32: cudaFuncSetAttribute");
-    hist_smem<true><<<(unsigned)blocks, kThreads, (size_t)smem, s>>>(counts, (uint32_t)nbins, keys1, n, (int)head,
-                                                                    replicas, dev->err_word);
-  } else {
-    e = cudaFuncSetAttribute(hist_smem<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return mk::fail_cuda(e, "mk_hist_u32: cudaFuncSetAttribute");
-    hist_smem<false><<<(unsigned)blocks, kThreads, (size_t)smem, s>>>(counts, (uint32_t)nbins, keys1, n, (int)head,
-                                                                     replicas, dev->err_word);
+  switch (t.unroll) {
+    case 1: return launch_smem<1>(blocks, smem, s, counts, nbins, keys1, n, (int)head, replicas, dev->err_word);
+    case 4: return launch_smem<4>(blocks, smem, s, counts, nbins, keys1, n, (int)head, replicas, dev->err_word);
+    case 8: return launch_smem<8>(blocks, smem, s, counts, nbins, keys1, n, (int)head, replicas, dev->err_word);
+    default: return launch_smem<2>(blocks, smem, s, counts, nbins, keys1, n, (int)head, replicas, dev->err_word);
   }
-  return mk::check_launch("mk_hist_u32: launch");
 }

@@ -54,6 +54,9 @@ int stream_workspace(Device* d, cudaStream_t s, size_t bytes, void** out, int sl
 // MK_WAIT_LIMIT_CYCLES overrides; default ~2 s at 1.9 GHz).
 unsigned long long wait_limit_cycles();
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (device, kernel).
+int allow_dynamic_smem(const void* kernel, size_t bytes);
+
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }

@@ -3,15 +3,15 @@
 // AcceleratedKernels runs a decoupled look-back scan; this is the same
 // single-pass scheme written for sm_100a, 8 bytes of HBM traffic per element.
 //
-//   * tiles of 4096 elements (256 threads x 16) are claimed in launch order
+//   * tiles of 8192 elements (256 threads x 32) are claimed in launch order
 //     from an atomic counter, so every predecessor of a tile is already
 //     running: waiting on it cannot deadlock;
 //   * a tile loads with coalesced 16-byte vectors through shared memory, scans
-//     each thread's 16 values and the 256 thread totals in fp64, publishes its
-//     aggregate (flag 1), then warp 0 looks back over 32 predecessors at a
-//     time: the nearest inclusive prefix (flag 2) plus the aggregates after it
-//     give the tile's exclusive prefix; the tile publishes its own inclusive
-//     prefix (flag 2) and writes its outputs;
+//     each thread's 32 values and the 256 thread totals in fp64, publishes its
+//     aggregate, then warp 0 looks back over 32 predecessors at a time: the
+//     nearest inclusive prefix plus the aggregates after it give the tile's
+//     exclusive prefix; the tile publishes its own inclusive prefix and writes
+//     its outputs.  Value and kind share one 64-bit word (see ScanState);
 //   * values are carried in fp64 and rounded to Float32 once, so each output
 //     is the correctly rounded prefix of the exact fp64 running value (max/min
 //     exact).  Sequential fp32 summation (Base.cumsum) can only be less
@@ -19,6 +19,8 @@
 //   * waits on predecessors are bounded (mk::wait_limit_cycles); a timeout
 //     raises ERRBIT_TIMEOUT and publishes a prefix anyway so no successor waits
 //     forever.
+#include <stdlib.h>
+
 #include "mk_common.cuh"
 #include "reduce_ops.cuh"
 
@@ -27,30 +29,45 @@ namespace {
 using namespace mk::rops;
 
 constexpr int kThreads = 256;
-constexpr int kPer = 16;
-constexpr int kTile = kThreads * kPer;
 
+// Per-tile state: one 64-bit word that is published with a single store, so
+// a reader needs one load and no fence.  EMPTY is an all-ones NaN pattern
+// (the workspace is memset to 0xFF); otherwise the word is an fp64 value whose
+// lowest mantissa bit is replaced by the kind: 0 = tile aggregate, 1 =
+// inclusive prefix.  Losing that bit (2^-52 relative) is far below the final
+// Float32 rounding.
 struct ScanState {
-  unsigned* counter;  // tile ticket
-  unsigned* flags;    // per tile: 0 empty, 1 aggregate, 2 inclusive prefix
-  double* agg;
-  double* inc;
+  unsigned* counter;              // tile ticket
+  unsigned long long* word;       // per tile
 };
+constexpr unsigned long long EMPTY = ~0ull;
+
+__device__ __forceinline__ unsigned long long pack(double v, unsigned kind) {
+  unsigned long long w = (__double_as_longlong(v) & ~1ull) | kind;
+  return w == EMPTY ? (EMPTY - 2ull) | kind : w;  // keep NaN, never EMPTY
+}
+__device__ __forceinline__ double unpack(unsigned long long w) { return __longlong_as_double(w & ~1ull); }
+
+__device__ __forceinline__ void publish(unsigned long long* p, unsigned long long w) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long peek(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
 
 __device__ __forceinline__ int pad(int i) { return i + (i >> 5); }
 
-__device__ __forceinline__ unsigned ld_flag(const unsigned* p) {
-  return *reinterpret_cast<const volatile unsigned*>(p);
-}
-
-template <int OP>
+template <int OP, int kPer>
 __global__ void __launch_bounds__(kThreads)
 scan_kernel(float* out, const float* x,  // may alias: a tile reads all of its input before writing
             int64_t n, double init, int exclusive,
             ScanState st, unsigned long long limit, unsigned* __restrict__ err) {
-  // one pad word per 32 floats: a thread's 16 consecutive values and a warp's
+  constexpr int kTile = kThreads * kPer;
+  // one pad word per 32 floats: a thread's consecutive values and a warp's
   // float4 columns both map to 32 distinct banks
-  __shared__ float buf[kTile + kTile / 32];
+  extern __shared__ float buf[];  // kTile + kTile / 32 floats
   __shared__ double warp_tot[kThreads / 32];
   __shared__ unsigned s_tile;
   __shared__ double s_prefix;
@@ -78,15 +95,14 @@ scan_kernel(float* out, const float* x,  // may alias: a tile reads all of its i
   }
   __syncthreads();
 
-  // per-thread inclusive scan of 16 values (fp64)
-  double v[kPer];
+  // per-thread total of its kPer values (fp64); the values are re-read from
+  // shared memory for the output pass, which keeps registers (and so
+  // occupancy) free for more tiles in flight
   double run = neutral<OP>();
-#pragma unroll
+#pragma unroll 8
   for (int j = 0; j < kPer; ++j) {
     const int idx = tid * kPer + j;
-    const double e = idx < cnt ? (double)buf[pad(idx)] : neutral<OP>();
-    run = combine<OP>(run, e);
-    v[j] = run;
+    if (idx < cnt) run = combine<OP>(run, (double)buf[pad(idx)]);
   }
   // block exclusive scan of thread totals
   double inc = run;
@@ -112,33 +128,25 @@ scan_kernel(float* out, const float* x,  // may alias: a tile reads all of its i
     if (t == 0) {
       prefix = init;
     } else {
-      if (lane == 0) {
-        st.agg[t] = block_total;
-        __threadfence();
-        atomicExch(st.flags + t, 1u);
-      }
+      if (lane == 0) publish(st.word + t, pack(block_total, 0u));
       double acc = neutral<OP>();
       int64_t j = t - 1 - lane;  // lane i looks at tile t-1-i
       bool found = false, timed_out = false;
       const long long t0 = clock64();
       while (!found) {
-        unsigned f = (j >= 0) ? ld_flag(st.flags + j) : 2u;
+        unsigned long long w = (j >= 0) ? peek(st.word + j) : pack(init, 1u);
         // wait (warp-uniformly) until every lane of the window sees a value
-        while (!__all_sync(0xffffffffu, f != 0u)) {
+        while (!__all_sync(0xffffffffu, w != EMPTY)) {
           if (__any_sync(0xffffffffu, (unsigned long long)(clock64() - t0) > limit)) {
             timed_out = true;
             break;
           }
-          if (j >= 0 && f == 0u) f = ld_flag(st.flags + j);
+          if (w == EMPTY) w = peek(st.word + j);
         }
         if (timed_out) break;
-        __threadfence();
-        double val;
-        if (j < 0) val = init;  // before tile 0: the initial value
-        else val = (f == 2u) ? __ldcg(st.inc + j) : __ldcg(st.agg + j);
-        const unsigned incl = __ballot_sync(0xffffffffu, f == 2u);
+        const unsigned incl = __ballot_sync(0xffffffffu, (w & 1ull) != 0ull);
         const int stop = incl ? __ffs(incl) - 1 : 32;  // nearest lane holding an inclusive prefix
-        double part = (lane <= stop) ? val : neutral<OP>();
+        double part = (lane <= stop) ? unpack(w) : neutral<OP>();
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) part = combine<OP>(part, __shfl_xor_sync(0xffffffffu, part, o));
         acc = combine<OP>(part, acc);
@@ -152,19 +160,19 @@ scan_kernel(float* out, const float* x,  // may alias: a tile reads all of its i
       prefix = acc;
     }
     if (lane == 0) {
-      st.inc[t] = combine<OP>(prefix, block_total);
-      __threadfence();
-      atomicExch(st.flags + t, 2u);
+      publish(st.word + t, pack(combine<OP>(prefix, block_total), 1u));
       s_prefix = prefix;
     }
   }
   __syncthreads();
-  const double pre = combine<OP>(s_prefix, texcl);
-#pragma unroll
+  double r = combine<OP>(s_prefix, texcl);
+#pragma unroll 8
   for (int j = 0; j < kPer; ++j) {
     const int idx = tid * kPer + j;
-    const double before = (j == 0) ? pre : combine<OP>(pre, v[j - 1]);
-    buf[pad(idx)] = (float)(exclusive ? before : combine<OP>(pre, v[j]));
+    const float e = buf[pad(idx)];
+    const double before = r;
+    if (idx < cnt) r = combine<OP>(r, (double)e);
+    buf[pad(idx)] = (float)(exclusive ? before : r);
   }
   __syncthreads();
   if (cnt == kTile && ((reinterpret_cast<uintptr_t>(out + base) & 15u) == 0)) {
@@ -179,6 +187,33 @@ scan_kernel(float* out, const float* x,  // may alias: a tile reads all of its i
   }
 }
 
+// elements per thread (tuning knob MK_TUNE_SCAN_PER: 16, 32 or 64)
+int scan_per() {
+  static int v = [] {
+    const char* e = getenv("MK_TUNE_SCAN_PER");
+    int p = e ? atoi(e) : 32;
+    return (p == 16 || p == 32 || p == 64) ? p : 32;
+  }();
+  return v;
+}
+
+template <int OP, int PER>
+int launch_per(int64_t tiles, size_t smem, cudaStream_t s, float* out, const float* x, int64_t n, double init,
+               int exclusive, ScanState st, unsigned long long limit, unsigned* err) {
+  int rc = mk::allow_dynamic_smem(reinterpret_cast<const void*>(scan_kernel<OP, PER>), smem);
+  if (rc != MK_OK) return rc;
+  scan_kernel<OP, PER><<<(unsigned)tiles, kThreads, smem, s>>>(out, x, n, init, exclusive, st, limit, err);
+  return MK_OK;
+}
+
+template <int OP>
+int launch(int per, int64_t tiles, size_t smem, cudaStream_t s, float* out, const float* x, int64_t n, double init,
+           int exclusive, ScanState st, unsigned long long limit, unsigned* err) {
+  if (per == 16) return launch_per<OP, 16>(tiles, smem, s, out, x, n, init, exclusive, st, limit, err);
+  if (per == 64) return launch_per<OP, 64>(tiles, smem, s, out, x, n, init, exclusive, st, limit, err);
+  return launch_per<OP, 32>(tiles, smem, s, out, x, n, init, exclusive, st, limit, err);
+}
+
 }  // namespace
 
 extern "C" int mk_accumulate_f32(float* out, const float* x, int64_t n, int op, double init, int exclusive,
@@ -188,26 +223,27 @@ extern "C" int mk_accumulate_f32(float* out, const float* x, int64_t n, int op, 
   if (op < MK_OP_ADD || op > MK_OP_MUL) return mk::fail(MK_ERR_INVALID, "mk_accumulate_f32: unknown op");
   if (n == 0) return MK_OK;
   if (!out || !x) return mk::fail(MK_ERR_INVALID, "mk_accumulate_f32: null pointer");
-  const int64_t tiles = mk::cdiv(n, kTile);
+  const int64_t tiles = mk::cdiv(n, (int64_t)kThreads * scan_per());
   if (tiles > (int64_t)UINT32_MAX / 2) return mk::fail(MK_ERR_INVALID, "mk_accumulate_f32: n too large");
   cudaStream_t s = mk::as_stream(stream);
-  // workspace: [counter | flags(tiles) | agg(tiles) | inc(tiles)], 256-byte aligned parts
-  const size_t flags_bytes = ((size_t)tiles * 4 + 255) & ~(size_t)255;
-  const size_t val_bytes = ((size_t)tiles * 8 + 255) & ~(size_t)255;
+  // workspace: [counter (256 B) | one state word per tile]
   void* ws = nullptr;
-  int rc = mk::stream_workspace(dev, s, 256 + flags_bytes + 2 * val_bytes, &ws, mk::WS_SCAN);
+  int rc = mk::stream_workspace(dev, s, 256 + (size_t)tiles * 8, &ws, mk::WS_SCAN);
   if (rc != MK_OK) return rc;
   char* b = static_cast<char*>(ws);
-  ScanState st{reinterpret_cast<unsigned*>(b), reinterpret_cast<unsigned*>(b + 256),
-               reinterpret_cast<double*>(b + 256 + flags_bytes), reinterpret_cast<double*>(b + 256 + flags_bytes + val_bytes)};
-  cudaError_t e = cudaMemsetAsync(b, 0, 256 + flags_bytes, s);  // ticket and flags start at zero
-  if (e != cudaSuccess) return mk::fail_cuda(e, "mk_accumulate_f32: clearing tile flags");
+  ScanState st{reinterpret_cast<unsigned*>(b), reinterpret_cast<unsigned long long*>(b + 256)};
+  cudaError_t e = cudaMemsetAsync(b, 0, 256, s);  // the ticket starts at zero
+  if (e == cudaSuccess) e = cudaMemsetAsync(b + 256, 0xFF, (size_t)tiles * 8, s);  // every tile EMPTY
+  if (e != cudaSuccess) return mk::fail_cuda(e, "mk_accumulate_f32: clearing tile state");
   const unsigned long long limit = mk::wait_limit_cycles();
+  const int per = scan_per();
+  const size_t smem = (size_t)(kThreads * per + kThreads * per / 32) * sizeof(float);
   switch (op) {
-    case MK_OP_ADD: scan_kernel<MK_OP_ADD><<<(unsigned)tiles, kThreads, 0, s>>>(out, x, n, init, exclusive, st, limit, dev->err_word); break;
-    case MK_OP_MAX: scan_kernel<MK_OP_MAX><<<(unsigned)tiles, kThreads, 0, s>>>(out, x, n, init, exclusive, st, limit, dev->err_word); break;
-    case MK_OP_MIN: scan_kernel<MK_OP_MIN><<<(unsigned)tiles, kThreads, 0, s>>>(out, x, n, init, exclusive, st, limit, dev->err_word); break;
-    default: scan_kernel<MK_OP_MUL><<<(unsigned)tiles, kThreads, 0, s>>>(out, x, n, init, exclusive, st, limit, dev->err_word); break;
+    case MK_OP_ADD: rc = launch<MK_OP_ADD>(per, tiles, smem, s, out, x, n, init, exclusive, st, limit, dev->err_word); break;
+    case MK_OP_MAX: rc = launch<MK_OP_MAX>(per, tiles, smem, s, out, x, n, init, exclusive, st, limit, dev->err_word); break;
+    case MK_OP_MIN: rc = launch<MK_OP_MIN>(per, tiles, smem, s, out, x, n, init, exclusive, st, limit, dev->err_word); break;
+    default: rc = launch<MK_OP_MUL>(per, tiles, smem, s, out, x, n, init, exclusive, st, limit, dev->err_word); break;
   }
+  if (rc != MK_OK) return rc;
   return mk::check_launch("mk_accumulate_f32: launch");
 }

@@ -450,8 +450,6 @@ int make_map(CUtensorMap* map, const float* base, uint64_t cols, uint64_t rows, 
   return MK_OK;
 }
 
-std::once_flag g_attr_once;
-cudaError_t g_attr_err = cudaSuccess;
 
 }  // namespace
 
@@ -502,10 +500,7 @@ int sgemm_impl(const char* name, bool full_k, float* C, const float* A, const fl
   CUtensorMap mapA, mapB;
   if ((rc = make_map(&mapA, A2, cols, (uint64_t)M, BM)) != MK_OK) return rc;
   if ((rc = make_map(&mapB, B2, cols, (uint64_t)N, BN)) != MK_OK) return rc;
-  std::call_once(g_attr_once, [] {
-    g_attr_err = cudaFuncSetAttribute(sgemm_tf32x3, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  });
-  if (g_attr_err != cudaSuccess) return mk::fail_cuda(g_attr_err, "mk_sgemm_3xtf32: cudaFuncSetAttribute");
+  if ((rc = mk::allow_dynamic_smem(reinterpret_cast<const void*>(sgemm_tf32x3), SMEM_BYTES)) != MK_OK) return rc;
   const int64_t tiles = mk::cdiv(N, BN) * mk::cdiv(M, BM);
   dim3 grid((unsigned)tiles);
   sgemm_tf32x3<<<grid, kThreads, SMEM_BYTES, s>>>(mapA, mapB, C, M, N, ldc, nkb, mk::wait_limit_cycles(),

@@ -411,3 +411,46 @@ int mlirb_mm_tiled16_f32(float* C, const float* A, const float* B, int64_t M, in
   }
   return OR_OK;
 }
+
+/* accumulate!(+) on MLIRBackend: AcceleratedKernels' block scan restated as
+ * blocks of 2W elements scanned per block in fp32 (OpenMP), block totals
+ * scanned sequentially, then a second parallel pass adding the block prefix. */
+int mlirb_cumsum_f32(float* out, const float* x, int64_t n, int W, float* block_tot) {
+  if (W < 1) return OR_ERR_INVALID;
+  const int64_t B = 2 * (int64_t)W;
+  const int64_t nb = (n + B - 1) / B;
+#pragma omp parallel for schedule(static)
+  for (int64_t b = 0; b < nb; ++b) {
+    float acc = 0.0f;
+    const int64_t e = (b + 1) * B < n ? (b + 1) * B : n;
+    for (int64_t i = b * B; i < e; ++i) out[i] = (acc += x[i]);
+    block_tot[b] = acc;
+  }
+  float run = 0.0f;
+  for (int64_t b = 0; b < nb; ++b) {
+    const float t = block_tot[b];
+    block_tot[b] = run;
+    run += t;
+  }
+#pragma omp parallel for schedule(static)
+  for (int64_t b = 1; b < nb; ++b) {
+    const float p = block_tot[b];
+    const int64_t e = (b + 1) * B < n ? (b + 1) * B : n;
+#pragma omp simd
+    for (int64_t i = b * B; i < e; ++i) out[i] += p;
+  }
+  return OR_OK;
+}
+
+/* sum(m; dims=1) on MLIRBackend for a column-major rows x cols Float32
+ * matrix: OpenMP over columns, fp32 accumulation per column. */
+void mlirb_sum_dims1_f32(float* out, const float* x, int64_t rows, int64_t cols) {
+#pragma omp parallel for schedule(static)
+  for (int64_t j = 0; j < cols; ++j) {
+    float acc = 0.0f;
+    const float* c = x + j * rows;
+#pragma omp simd reduction(+ : acc)
+    for (int64_t i = 0; i < rows; ++i) acc += c[i];
+    out[j] = acc;
+  }
+}
