@@ -49,5 +49,35 @@ __device__ __forceinline__ double neutral() {
   return INFINITY;
 }
 
+// fp32 forms (same semantics) for kernels that combine Float32 values.
+__device__ __forceinline__ float jl_max32(float a, float b) {
+  if (a != a) return a;
+  if (b != b) return b;
+  if (a == b) return signbit(a) ? b : a;
+  return a > b ? a : b;
+}
+__device__ __forceinline__ float jl_min32(float a, float b) {
+  if (a != a) return a;
+  if (b != b) return b;
+  if (a == b) return signbit(a) ? a : b;
+  return a < b ? a : b;
+}
+
+template <int OP>
+__device__ __forceinline__ float combine32(float a, float b) {
+  if (OP == MK_OP_ADD) return __fadd_rn(a, b);
+  if (OP == MK_OP_MUL) return __fmul_rn(a, b);
+  if (OP == MK_OP_MAX) return jl_max32(a, b);
+  return jl_min32(a, b);
+}
+
+template <int OP>
+__device__ __forceinline__ float neutral32() {
+  if (OP == MK_OP_ADD) return 0.0f;
+  if (OP == MK_OP_MUL) return 1.0f;
+  if (OP == MK_OP_MAX) return -INFINITY;
+  return INFINITY;
+}
+
 }  // namespace rops
 }  // namespace mk

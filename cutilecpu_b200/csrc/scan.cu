@@ -12,10 +12,11 @@
 //     nearest inclusive prefix plus the aggregates after it give the tile's
 //     exclusive prefix; the tile publishes its own inclusive prefix and writes
 //     its outputs.  Value and kind share one 64-bit word (see ScanState);
-//   * values are carried in fp64 and rounded to Float32 once, so each output
-//     is the correctly rounded prefix of the exact fp64 running value (max/min
-//     exact).  Sequential fp32 summation (Base.cumsum) can only be less
-//     accurate;
+//   * carries between threads and tiles are fp64; inside a thread the 32
+//     values are combined in fp32 (a pairwise tree for the total, a running
+//     sum for the outputs), so each output is within a few ulp of the exact
+//     prefix, relative to the running sum of magnitudes (max/min exact).
+//     Sequential fp32 summation (Base.cumsum) errs by up to n ulp;
 //   * waits on predecessors are bounded (mk::wait_limit_cycles); a timeout
 //     raises ERRBIT_TIMEOUT and publishes a prefix anyway so no successor waits
 //     forever.
@@ -95,14 +96,23 @@ scan_kernel(float* out, const float* x,  // may alias: a tile reads all of its i
   }
   __syncthreads();
 
-  // per-thread total of its kPer values (fp64); the values are re-read from
-  // shared memory for the output pass, which keeps registers (and so
-  // occupancy) free for more tiles in flight
-  double run = neutral<OP>();
-#pragma unroll 8
-  for (int j = 0; j < kPer; ++j) {
-    const int idx = tid * kPer + j;
-    if (idx < cnt) run = combine<OP>(run, (double)buf[pad(idx)]);
+  // per-thread total of its kPer values: an fp32 pairwise tree (relative
+  // error <= log2(kPer) ulp of the sum of magnitudes), widened to fp64 for
+  // the carries.  The values are re-read from shared memory for the output
+  // pass, which keeps registers (and so occupancy) free for more tiles.
+  double run;
+  {
+    float v[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int idx = tid * kPer + j;
+      v[j] = idx < cnt ? buf[pad(idx)] : neutral32<OP>();
+    }
+#pragma unroll
+    for (int w = 1; w < kPer; w <<= 1)
+#pragma unroll
+      for (int j = 0; j + w < kPer; j += 2 * w) v[j] = combine32<OP>(v[j], v[j + w]);
+    run = (double)v[0];
   }
   // block exclusive scan of thread totals
   double inc = run;
@@ -165,14 +175,16 @@ scan_kernel(float* out, const float* x,  // may alias: a tile reads all of its i
     }
   }
   __syncthreads();
-  double r = combine<OP>(s_prefix, texcl);
+  // output: the fp64 thread prefix rounded once to fp32, then an fp32
+  // running combination of the thread's own values (<= kPer terms)
+  const float pre = (float)combine<OP>(s_prefix, texcl);
+  float loc = neutral32<OP>();
 #pragma unroll 8
   for (int j = 0; j < kPer; ++j) {
     const int idx = tid * kPer + j;
-    const float e = buf[pad(idx)];
-    const double before = r;
-    if (idx < cnt) r = combine<OP>(r, (double)e);
-    buf[pad(idx)] = (float)(exclusive ? before : r);
+    const float before = combine32<OP>(pre, loc);
+    if (idx < cnt) loc = combine32<OP>(loc, buf[pad(idx)]);
+    buf[pad(idx)] = exclusive ? before : combine32<OP>(pre, loc);
   }
   __syncthreads();
   if (cnt == kTile && ((reinterpret_cast<uintptr_t>(out + base) & 15u) == 0)) {
