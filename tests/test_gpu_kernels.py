@@ -280,3 +280,29 @@ def test_tiled16_golden(L):
     assert L.mk_matmul_tiled16_f32(Cd.data_ptr(), A.data_ptr(), B.data_ptr(), 256, 256, 256, 256, 256, 256,
                                    stream()) == 0
     np.testing.assert_allclose(host(Cd).reshape((256, 256), order="F"), g["C"], rtol=1e-5)
+
+
+# large sources: mixed valid/invalid indices into a 128-256 MiB `a`, and the
+# full benchmark configuration (2^27 into 2^27)
+@pytest.mark.parametrize("n,na", [((1 << 22) + 3, (1 << 25) + 7), (1 << 23, 1 << 26)])
+def test_gather_large_vs_oracle(L, n, na):
+    r = np.random.Generator(np.random.Philox(n ^ na))
+    a_h = r.random(na, dtype=np.float32)
+    idx_h = r.integers(1, na + 1, size=n, dtype=np.int32)
+    idx_h[::100_003] = 0          # a few out-of-range indices
+    idx_h[7::200_003] = na + 1
+    got = gather_dev(L, a_h, idx_h)
+    want, rc = oracle.gather(a_h, idx_h)
+    assert rc == -5
+    np.testing.assert_array_equal(got, want)
+    assert poll(L) == _lib.MK_ERR_DEVICE_FAULT
+
+
+def test_gather_full_size(L):
+    from cutilecpu_b200 import workloads
+    n = na = 1 << 27
+    a_h = workloads.uniform01(na, stream=20)
+    idx_h = workloads.indices1(n, na, stream=21)
+    got = gather_dev(L, a_h, idx_h)
+    np.testing.assert_array_equal(got, a_h[idx_h.astype(np.int64) - 1])
+    assert poll(L) == 0
