@@ -12,11 +12,13 @@ from .kernels import Kernel, KernelFunction, gather, histogram, mm_naive, mm_til
 from .reductions import (Broadcasted, abs2, accumulate, cumsum, count, identity, mapreduce, mapreducedim, maximum, minimum,
                      positive, prod, reduce, sum)
 from . import distributed, reductions
+from .pool import aligned_array, pointer_aligned, pool_allocate, pool_stats, pool_trim
 
 __all__ = [
     "KernelException", "MLIRKernelsError", "Array", "MLIRArray", "MLIRCUDABackend", "allocate",
     "copyto", "functional", "get_backend", "launch_config", "ones", "supports_atomics", "synchronize",
     "zeros", "Kernel", "KernelFunction", "gather", "histogram", "mm_naive", "mm_tiled", "mm_tiled_simt", "mul", "vadd", "Broadcasted",
     "abs2", "accumulate", "cumsum", "count", "identity", "mapreduce", "mapreducedim", "maximum", "minimum", "positive", "prod",
-    "reduce", "sum", "distributed",
+    "reduce", "sum", "distributed", "aligned_array", "pointer_aligned", "pool_allocate", "pool_stats",
+    "pool_trim",
 ]

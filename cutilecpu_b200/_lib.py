@@ -39,6 +39,12 @@ SIGNATURES = {
     "mk_sgemm_3xtf32": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "mk_sgemm_f32": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "mk_matmul_tiled16_f32": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "mk_pool_alloc_device": (_int, [C.POINTER(C.c_void_p), C.c_size_t, _vp]),
+    "mk_pool_free_device": (_int, [_vp, _vp]),
+    "mk_host_alloc_aligned": (_int, [C.POINTER(C.c_void_p), C.c_size_t, C.c_size_t]),
+    "mk_host_free": (_int, [_vp]),
+    "mk_pool_stats": (_int, [C.POINTER(C.c_size_t)] * 4),
+    "mk_pool_trim": (_int, []),
 }
 
 

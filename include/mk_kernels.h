@@ -177,6 +177,28 @@ MK_API int mk_matmul_tiled16_f32(float* C, const float* A, const float* B,
                           int64_t M, int64_t N, int64_t K,
                           int64_t lda, int64_t ldb, int64_t ldc, void* stream);
 
+/* ---- memory pools -------------------------------------------------------
+ * Device memory from a per-device stream-ordered pool that keeps freed memory
+ * cached (allocation and free are ordered on `stream`); replaces the CUDA.jl
+ * pool behind KA.allocate(::MLIRCUDABackend, T, dims) (ext/MLIRCUDAExt.jl:140). */
+#include <stddef.h>
+MK_API int mk_pool_alloc_device(void** ptr, size_t bytes, void* stream);
+MK_API int mk_pool_free_device(void* ptr, void* stream);
+
+/* Pinned (page-locked) host memory, cached per power-of-two size class and
+ * page-aligned, with the alignment rules of aligned_array
+ * (src/allocator.jl:32-61): alignment must be positive, a power of two and a
+ * multiple of sizeof(void*) (here also <= 4096); violations return
+ * MK_ERR_INVALID with the reference's message.  The host side of fast
+ * H2D/D2H copies. */
+MK_API int mk_host_alloc_aligned(void** ptr, size_t bytes, size_t alignment);
+MK_API int mk_host_free(void* ptr);
+
+/* Pool occupancy (any out pointer may be NULL) and release of cached memory. */
+MK_API int mk_pool_stats(size_t* device_reserved, size_t* device_used, size_t* pinned_live,
+                         size_t* pinned_cached);
+MK_API int mk_pool_trim(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -93,3 +93,19 @@ def test_row_block_aligned():
 
 def test_world_without_process_group():
     assert distributed.world() == (0, 1)
+
+
+@pytest.mark.parametrize("bad,msg", [(0, "positive"), (-8, "positive"), (24, "power of two"), (4, "multiple of sizeof")])
+def test_aligned_array_rejects_bad_alignment(bad, msg):
+    # src/allocator.jl:52-61 checks, raised before any allocation
+    with pytest.raises(ValueError, match=msg):
+        mk.aligned_array("Float32", 16, alignment=bad)
+
+
+def test_c_abi_alignment_checks_without_gpu():
+    import ctypes as C
+    L = _lib.lib()
+    p = C.c_void_p()
+    assert L.mk_host_alloc_aligned(C.byref(p), 64, 24) == _lib.MK_ERR_INVALID
+    assert b"power of two" in L.mk_last_error()
+    assert L.mk_host_alloc_aligned(C.byref(p), 64, 0) == _lib.MK_ERR_INVALID
