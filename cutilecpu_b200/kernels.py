@@ -152,11 +152,13 @@ def _launch_histogram(args, nd, wg, stream) -> None:
     if len(args) != 2:
         raise _lib.MLIRKernelsError("histogram!(bins, keys): expected 2 arguments")
     n = nd[0]
-    bins = _need(args[0], "bins", ("UInt32", "Int32"), 1, "histogram!")
-    keys = _need(args[1], "keys", ("Int32",), n, "histogram!")
+    bins = _need(args[0], "bins", ("UInt32", "Int32", "Int64", "Float32"), 1, "histogram!")
+    keys = _need(args[1], "keys", ("Int32", "Int64"), n, "histogram!")
     if bins.length > 2**31 - 1:
         raise _lib.MLIRKernelsError("histogram!: too many bins")
-    _lib.check(_lib.lib().mk_hist_u32(bins.pointer(), bins.length, keys.pointer(), n, stream),
+    bin_type = {"UInt32": 0, "Int32": 0, "Int64": 1, "Float32": 2}[bins.eltype]
+    key_type = 0 if keys.eltype == "Int32" else 1
+    _lib.check(_lib.lib().mk_hist(bins.pointer(), bin_type, bins.length, keys.pointer(), key_type, n, stream),
                "histogram!")
 
 

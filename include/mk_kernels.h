@@ -170,6 +170,21 @@ MK_API int mk_sgemm_f32(float* C, const float* A, const float* B,
                         int64_t M, int64_t N, int64_t K,
                         int64_t lda, int64_t ldb, int64_t ldc, void* stream);
 
+/* Histogram with the element types of the reference's other histogram forms:
+ * bins of type bin_type (MK_BIN_U32: UInt32/Int32 bits, wrap-around;
+ * MK_BIN_I64: Int64, two's complement; MK_BIN_F32: Float32, exact while a bin
+ * stays below 2^24), 1-based keys of type key_type (MK_KEY_I32 / MK_KEY_I64).
+ * Same accumulation and error rules as mk_hist_u32.  Covers the KA example of
+ * test/test_gpu_simt.jl:49-73 (Int keys, Int bins) and the Float32 bins of
+ * test/test_ka_cpu.jl:16-19, 67-79. */
+#define MK_BIN_U32 0
+#define MK_BIN_I64 1
+#define MK_BIN_F32 2
+#define MK_KEY_I32 0
+#define MK_KEY_I64 1
+MK_API int mk_hist(void* bins, int bin_type, int32_t nbins, const void* keys1, int key_type, int64_t n,
+                   void* stream);
+
 /* The reference's own algorithm on CUDA cores: one output per thread, 16x16
  * shared-memory tiles, K % 16 ignored (examples/tiled_matmul.jl:28-48).  Kept
  * as the SIMT comparison point for the tensor-core path; same argument rules. */

@@ -306,3 +306,41 @@ def test_gather_full_size(L):
     got = gather_dev(L, a_h, idx_h)
     np.testing.assert_array_equal(got, a_h[idx_h.astype(np.int64) - 1])
     assert poll(L) == 0
+
+
+# the reference's other histogram forms: Int keys / Int bins (KA example,
+# test/test_gpu_simt.jl:353-359) and Float32 bins (test/test_ka_cpu.jl:67-79)
+def test_hist_ka_example_int64_keys_and_bins(L):
+    import cutilecpu_b200 as mk
+    g = golden("hist_ka_4096_256")
+    keys = mk.MLIRArray(g["keys"].astype(np.int64))
+    bins = mk.zeros(mk.MLIRCUDABackend(), "Int64", 256)
+    mk.histogram(mk.MLIRCUDABackend(), (256,))(bins, keys, ndrange=4096)
+    mk.synchronize(mk.MLIRCUDABackend())
+    np.testing.assert_array_equal(mk.Array(bins), g["counts"].astype(np.int64))
+
+
+@pytest.mark.parametrize("name", ["hist_mod_4096_8", "hist_one_65536"])
+def test_hist_float32_bins(L, name):
+    import cutilecpu_b200 as mk
+    g = golden(name)
+    bins = mk.zeros(mk.MLIRCUDABackend(), "Float32", int(g["nbins"]))
+    mk.histogram(mk.MLIRCUDABackend(), 16)(bins, mk.MLIRArray(g["keys"]), ndrange=g["keys"].size)
+    np.testing.assert_array_equal(mk.Array(bins), g["counts"].astype(np.float32))
+
+
+@pytest.mark.parametrize("bin_type,np_t", [(1, np.int64), (2, np.float32)])
+@pytest.mark.parametrize("key_type,key_t", [(0, np.int32), (1, np.int64)])
+@pytest.mark.parametrize("nbins", [7, 4096, 100_000])
+def test_hist_types_vs_oracle(L, bin_type, np_t, key_type, key_t, nbins):
+    r = np.random.Generator(np.random.Philox(nbins + 3 * bin_type + key_type))
+    keys = r.integers(1, nbins + 1, size=200_003, dtype=np.int32)
+    keys[::50_001] = nbins + 2  # out of range
+    kd = torch.from_numpy(keys.astype(key_t)).cuda()
+    start = np.arange(nbins, dtype=np_t) % 5
+    bd = torch.from_numpy(start.copy()).cuda()
+    assert L.mk_hist(bd.data_ptr(), bin_type, nbins, kd.data_ptr() + kd.element_size(), key_type,
+                     keys.size - 1, stream()) == 0
+    want = oracle.hist(keys[1:], nbins)[0].astype(np_t) + start
+    np.testing.assert_array_equal(host(bd), want)
+    assert poll(L) == _lib.MK_ERR_DEVICE_FAULT
