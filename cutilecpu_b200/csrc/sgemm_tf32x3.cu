@@ -22,14 +22,14 @@
 //                  N=256, K=8): hi.hi, hi.lo, lo.hi over the two k-halves,
 //                  addressed by offsetting the descriptor start inside the
 //                  swizzle atom; tcgen05.commit frees the stage;
-//       warps 2-9  epilogue: the tensor core accumulates each chunk of 128 k
-//                  (8 k-blocks) afresh into one of two 256-column TMEM buffers;
+//       warps 2-9  epilogue: the tensor core accumulates each chunk of 256 k
+//                  (16 k-blocks) afresh into one of two 256-column TMEM buffers;
 //                  the epilogue warps (each a 32-lane quarter x 128 columns)
 //                  drain a finished chunk with tcgen05.ld 32x32b and add it into
 //                  fp32 registers with round-to-nearest, while the MMAs of the
 //                  next chunk run into the other buffer.  The tensor core's
 //                  internal fp32 accumulation is biased (it does not round to
-//                  nearest); bounding it to 128 terms keeps the K=8192 result
+//                  nearest); bounding it to 256 terms keeps the K=8192 result
 //                  within 1e-5 of fp64.  Finally coalesced column-major stores.
 // Every mbarrier wait is bounded (mk::wait_limit_cycles); a timeout raises
 // ERRBIT_TIMEOUT in the device error word, stops the other roles, drains the
@@ -43,6 +43,10 @@
 
 #include "mk_common.cuh"
 
+#ifndef MK_SGEMM_CHUNK_KB
+#define MK_SGEMM_CHUNK_KB 16
+#endif
+
 namespace {
 
 constexpr int BM = 128;
@@ -55,7 +59,7 @@ constexpr int B_STAGE = BN * ROWF * 4;       // 32 KiB
 constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
 constexpr int EPI_WARPS = 8;
 constexpr int kThreads = 32 * (2 + EPI_WARPS);  // producer, MMA, 8 epilogue warps
-constexpr int CHUNK_KB = 8;                      // k-blocks per TMEM accumulation chunk (128 k)
+constexpr int CHUNK_KB = MK_SGEMM_CHUNK_KB;                      // k-blocks per TMEM accumulation chunk (256 k)
 constexpr uint32_t TMEM_COLS = 2 * BN;           // two 256-column accumulators
 constexpr int GROUP_M = 16;                      // tile-rows per raster group
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
