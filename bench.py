@@ -168,17 +168,23 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             self.x_host = workloads.uniform_pm1(n, stream=1 + 100 * rank)
             self.x = mk.MLIRArray(self.x_host)
             self.out = torch.empty(1, dtype=torch.float64, device="cuda")
+            self.peer = distributed.PeerReduce() if world > 1 else None
             self.units_per_step = 4.0 * n
             self.h2d_bytes, self.d2h_bytes = 4 * n, 8
             self.config = {"workload": "mapreduce sum(x.^2), Float32 x ~ U[-1,1), n=2^28 per GPU "
-                                       "(configs[1]); fused single pass, fp64 accumulation",
+                                       "(configs[1]); fused single pass, fp64 accumulation; N>1: partials "
+                                       "exchanged over NVLink peer memory inside the same kernel",
                            "n_per_gpu": n, "l2": "input (1 GiB) larger than L2; no flush"}
 
         def launch(self):
-            _lib.check(L.mk_sum_sq_f32(self.out.data_ptr(), self.x.pointer(), self.n, stream()), "sum_sq")
+            if self.peer is not None:  # fused: local reduction + NVLink exchange in one launch
+                _lib.check(L.mk_mapreduce_f32_allreduce(self.out.data_ptr(), self.x.pointer(), self.n, 1, 0, 0.0,
+                                                        stream()), "sum_sq allreduce")
+            else:
+                _lib.check(L.mk_sum_sq_f32(self.out.data_ptr(), self.x.pointer(), self.n, stream()), "sum_sq")
 
         def combine(self):
-            distributed.combine_partial(self.out, "add")
+            pass  # the exchange is inside the kernel
 
         def check(self):
             import oracle
@@ -193,8 +199,10 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
 
         def e2e_step(self):
             mk.copyto(be, self.xd, self.pinned)
-            res = mk.reductions.mapreduce_device(mk.abs2, operator.add, self.xd)
-            distributed.combine_partial(res, "add")
+            if self.peer is not None:
+                res = self.peer(self.xd, "abs2", "add")
+            else:
+                res = mk.reductions.mapreduce_device(mk.abs2, operator.add, self.xd)
             return res.item()
 
         def cpu_sample(self, threads):

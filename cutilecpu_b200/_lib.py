@@ -40,6 +40,11 @@ SIGNATURES = {
     "mk_sgemm_3xtf32": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "mk_sgemm_f32": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "mk_matmul_tiled16_f32": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "mk_peer_handle_size": (_int, []),
+    "mk_peer_create": (_int, [_int, _int, _vp]),
+    "mk_peer_connect": (_int, [_vp]),
+    "mk_peer_destroy": (_int, []),
+    "mk_mapreduce_f32_allreduce": (_int, [_vp, _vp, _i64, _int, _int, _f64, _vp]),
     "mk_pool_alloc_device": (_int, [C.POINTER(C.c_void_p), C.c_size_t, _vp]),
     "mk_pool_free_device": (_int, [_vp, _vp]),
     "mk_host_alloc_aligned": (_int, [C.POINTER(C.c_void_p), C.c_size_t, C.c_size_t]),

@@ -25,6 +25,7 @@
 #include <string>
 
 #include "mk_common.cuh"
+#include "peer.cuh"
 #include "reduce_ops.cuh"
 
 namespace {
@@ -76,13 +77,46 @@ __device__ __forceinline__ double block_reduce(double v, double* smem) {
   return v;  // valid in thread 0
 }
 
+// Multi-GPU exchange (one thread): publish this rank's partial into every
+// rank's mailbox over NVLink, then wait (bounded) for every rank's partial of
+// this epoch and fold them in rank order, so all ranks get the same value.
+template <int OP>
+__device__ double exchange(double mine, const mk::PeerArgs& peer, unsigned* err) {
+  const int par = (int)(peer.epoch & 1ull);
+  for (int p = 0; p < peer.world; ++p)
+    asm volatile("st.relaxed.sys.global.f64 [%0], %1;" ::"l"(peer.slots[p] + par * MK_MAX_PEERS + peer.rank),
+                 "d"(mine)
+                 : "memory");
+  __threadfence_system();
+  for (int p = 0; p < peer.world; ++p)
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(peer.flags[p] + peer.rank), "l"(peer.epoch) : "memory");
+  const unsigned long long* my_flags = peer.flags[peer.rank];
+  const double* my_slots = peer.slots[peer.rank] + par * MK_MAX_PEERS;
+  const long long t0 = clock64();
+  double acc = neutral<OP>();
+  for (int q = 0; q < peer.world; ++q) {
+    unsigned long long f;
+    do {
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(f) : "l"(my_flags + q) : "memory");
+      if (f < peer.epoch && (unsigned long long)(clock64() - t0) > peer.limit) {
+        atomicOr(err, mk::ERRBIT_TIMEOUT);  // a rank never arrived: report, fold what is there
+        break;
+      }
+    } while (f < peer.epoch);
+    double v;
+    asm volatile("ld.relaxed.sys.global.f64 %0, [%1];" : "=d"(v) : "l"(my_slots + q) : "memory");
+    acc = combine<OP>(acc, v);
+  }
+  return acc;
+}
+
 // x: base pointer; the first `head` (0..3) elements precede the first 16-byte
 // boundary and are folded by the first `head` threads, like the <4 tail.
 template <int F, int OP>
 __global__ void __launch_bounds__(kThreads)
 mapreduce_kernel(const float* __restrict__ x, int64_t n, int head, double init,
                  double* __restrict__ partials, unsigned* __restrict__ ticket,
-                 double* __restrict__ out) {
+                 double* __restrict__ out, const mk::PeerArgs peer, unsigned* __restrict__ err) {
   __shared__ double smem[kThreads / 32];
   __shared__ bool is_last;
   const int64_t tid = (int64_t)blockIdx.x * kThreads + threadIdx.x;
@@ -133,25 +167,27 @@ mapreduce_kernel(const float* __restrict__ x, int64_t n, int head, double init,
   __syncthreads();  // smem reuse
   v = block_reduce<OP>(v, smem);
   if (threadIdx.x == 0) {
-    out[0] = combine<OP>(init, v);
     *ticket = 0u;  // re-arm for the next reduction on this stream
+    if (peer.world > 0) v = exchange<OP>(v, peer, err);
+    out[0] = combine<OP>(init, v);
   }
 }
 
 template <int F, int OP>
 void launch(unsigned blocks, cudaStream_t s, const float* x, int64_t n, int head, double init,
-            const mk::ReduceScratch& rs, double* out) {
-  mapreduce_kernel<F, OP><<<blocks, kThreads, 0, s>>>(x, n, head, init, rs.partials, rs.ticket, out);
+            const mk::ReduceScratch& rs, double* out, const mk::PeerArgs& peer, unsigned* err) {
+  mapreduce_kernel<F, OP><<<blocks, kThreads, 0, s>>>(x, n, head, init, rs.partials, rs.ticket, out, peer, err);
 }
 
 template <int F>
 int dispatch_op(int op, unsigned blocks, cudaStream_t s, const float* x, int64_t n, int head,
-                double init, const mk::ReduceScratch& rs, double* out) {
+                double init, const mk::ReduceScratch& rs, double* out,
+                const mk::PeerArgs& peer = mk::PeerArgs(), unsigned* err = nullptr) {
   switch (op) {
-    case MK_OP_ADD: launch<F, MK_OP_ADD>(blocks, s, x, n, head, init, rs, out); break;
-    case MK_OP_MAX: launch<F, MK_OP_MAX>(blocks, s, x, n, head, init, rs, out); break;
-    case MK_OP_MIN: launch<F, MK_OP_MIN>(blocks, s, x, n, head, init, rs, out); break;
-    case MK_OP_MUL: launch<F, MK_OP_MUL>(blocks, s, x, n, head, init, rs, out); break;
+    case MK_OP_ADD: launch<F, MK_OP_ADD>(blocks, s, x, n, head, init, rs, out, peer, err); break;
+    case MK_OP_MAX: launch<F, MK_OP_MAX>(blocks, s, x, n, head, init, rs, out, peer, err); break;
+    case MK_OP_MIN: launch<F, MK_OP_MIN>(blocks, s, x, n, head, init, rs, out, peer, err); break;
+    case MK_OP_MUL: launch<F, MK_OP_MUL>(blocks, s, x, n, head, init, rs, out, peer, err); break;
     default: return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: unknown op");
   }
   return MK_OK;
@@ -168,9 +204,10 @@ int blocks_per_sm() {
 
 }  // namespace
 
-extern "C" int mk_mapreduce_f32(double* out_dev, const float* x, int64_t n, int f, int op,
-                                double init, void* stream) {
-  MK_ENTRY_DEVICE(dev);
+namespace {
+
+int mapreduce_impl(mk::Device* dev, double* out_dev, const float* x, int64_t n, int f, int op, double init,
+                   void* stream, const mk::PeerArgs& peer) {
   if (n < 0) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: n must be >= 0");
   if (!out_dev || (n > 0 && !x)) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: null pointer");
   if (f < MK_F_IDENTITY || f > MK_F_GT0) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: unknown f");
@@ -191,13 +228,30 @@ extern "C" int mk_mapreduce_f32(double* out_dev, const float* x, int64_t n, int 
   if (cap > mk::kMaxReduceBlocks) cap = mk::kMaxReduceBlocks;
   unsigned blocks = (unsigned)(want < 1 ? 1 : (want > cap ? cap : want));
   switch (f) {
-    case MK_F_IDENTITY: rc = dispatch_op<MK_F_IDENTITY>(op, blocks, s, x, n, head, init, rs, out_dev); break;
-    case MK_F_ABS2: rc = dispatch_op<MK_F_ABS2>(op, blocks, s, x, n, head, init, rs, out_dev); break;
-    case MK_F_ABS: rc = dispatch_op<MK_F_ABS>(op, blocks, s, x, n, head, init, rs, out_dev); break;
-    default: rc = dispatch_op<MK_F_GT0>(op, blocks, s, x, n, head, init, rs, out_dev); break;
+    case MK_F_IDENTITY: rc = dispatch_op<MK_F_IDENTITY>(op, blocks, s, x, n, head, init, rs, out_dev, peer, dev->err_word); break;
+    case MK_F_ABS2: rc = dispatch_op<MK_F_ABS2>(op, blocks, s, x, n, head, init, rs, out_dev, peer, dev->err_word); break;
+    case MK_F_ABS: rc = dispatch_op<MK_F_ABS>(op, blocks, s, x, n, head, init, rs, out_dev, peer, dev->err_word); break;
+    default: rc = dispatch_op<MK_F_GT0>(op, blocks, s, x, n, head, init, rs, out_dev, peer, dev->err_word); break;
   }
   if (rc != MK_OK) return rc;
   return mk::check_launch("mk_mapreduce_f32: launch");
+}
+
+}  // namespace
+
+extern "C" int mk_mapreduce_f32(double* out_dev, const float* x, int64_t n, int f, int op, double init,
+                                void* stream) {
+  MK_ENTRY_DEVICE(dev);
+  return mapreduce_impl(dev, out_dev, x, n, f, op, init, stream, mk::PeerArgs());
+}
+
+extern "C" int mk_mapreduce_f32_allreduce(double* out_dev, const float* x, int64_t n, int f, int op, double init,
+                                          void* stream) {
+  MK_ENTRY_DEVICE(dev);
+  mk::PeerArgs peer;
+  int rc = mk::peer_args_next(dev, &peer);
+  if (rc != MK_OK) return rc;
+  return mapreduce_impl(dev, out_dev, x, n, f, op, init, stream, peer);
 }
 
 extern "C" int mk_sum_sq_f32(double* out_dev, const float* x, int64_t n, void* stream) {

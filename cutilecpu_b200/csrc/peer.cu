@@ -1,0 +1,116 @@
+// peer.cu — set-up of the peer mailboxes (see peer.cuh).  One process per
+// GPU: each rank creates its mailbox, the host side exchanges the CUDA IPC
+// handles (torch.distributed all_gather in the Python layer), and every rank
+// maps the others' mailboxes.  Epochs start at 1 and only grow, so flags never
+// need resetting; a rank is at most one epoch ahead of any peer (it cannot
+// finish epoch e+1 without every peer's epoch-e+1 partial), which is why two
+// parity slots suffice.
+#include <cstring>
+#include <mutex>
+
+#include "peer.cuh"
+
+namespace {
+
+struct Mailbox {
+  int world = 0, rank = -1;
+  void* local = nullptr;
+  void* peers[MK_MAX_PEERS] = {};
+  bool opened[MK_MAX_PEERS] = {};
+  unsigned long long epoch = 0;
+  bool connected = false;
+};
+
+std::mutex g_mu;
+Mailbox g_box[64];
+
+}  // namespace
+
+namespace mk {
+
+int peer_args_next(Device* dev, PeerArgs* out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Mailbox& m = g_box[dev->id];
+  if (!m.connected) return fail(MK_ERR_INVALID, "peer mailbox of this device is not connected (mk_peer_connect)");
+  PeerArgs a;
+  a.world = m.world;
+  a.rank = m.rank;
+  a.epoch = ++m.epoch;
+  a.limit = wait_limit_cycles();
+  for (int p = 0; p < m.world; ++p) {
+    char* base = static_cast<char*>(m.peers[p]);
+    a.slots[p] = reinterpret_cast<double*>(base);
+    a.flags[p] = reinterpret_cast<unsigned long long*>(base + kMailboxSlotsBytes);
+  }
+  *out = a;
+  return MK_OK;
+}
+
+}  // namespace mk
+
+extern "C" int mk_peer_create(int world, int rank, void* handle_out) {
+  MK_ENTRY_DEVICE(dev);
+  if (world < 2 || world > MK_MAX_PEERS || rank < 0 || rank >= world)
+    return mk::fail(MK_ERR_INVALID, "mk_peer_create: need 2 <= world <= 8 and 0 <= rank < world");
+  if (!handle_out) return mk::fail(MK_ERR_INVALID, "mk_peer_create: null handle buffer");
+  std::lock_guard<std::mutex> lk(g_mu);
+  Mailbox& m = g_box[dev->id];
+  if (m.local) return mk::fail(MK_ERR_INVALID, "mk_peer_create: mailbox already exists (mk_peer_destroy first)");
+  cudaError_t e = cudaMalloc(&m.local, mk::kMailboxBytes);
+  if (e == cudaSuccess) e = cudaMemset(m.local, 0, mk::kMailboxBytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, m.local);
+  if (e != cudaSuccess) {
+    if (m.local) cudaFree(m.local);
+    m.local = nullptr;
+    return mk::fail_cuda(e, "mk_peer_create");
+  }
+  std::memcpy(handle_out, &h, sizeof(h));
+  m.world = world;
+  m.rank = rank;
+  m.epoch = 0;
+  m.connected = false;
+  return MK_OK;
+}
+
+extern "C" int mk_peer_handle_size(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int mk_peer_connect(const void* handles) {
+  MK_ENTRY_DEVICE(dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  Mailbox& m = g_box[dev->id];
+  if (!m.local) return mk::fail(MK_ERR_INVALID, "mk_peer_connect: no mailbox (mk_peer_create first)");
+  if (!handles) return mk::fail(MK_ERR_INVALID, "mk_peer_connect: null handles");
+  const char* hb = static_cast<const char*>(handles);
+  for (int p = 0; p < m.world; ++p) {
+    if (p == m.rank) {
+      m.peers[p] = m.local;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, hb + (size_t)p * sizeof(h), sizeof(h));
+    void* ptr = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return mk::fail_cuda(e, "mk_peer_connect: cudaIpcOpenMemHandle");
+    m.peers[p] = ptr;
+    m.opened[p] = true;
+  }
+  m.connected = true;
+  return MK_OK;
+}
+
+extern "C" int mk_peer_destroy(void) {
+  MK_ENTRY_DEVICE(dev);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return mk::fail_cuda(e, "mk_peer_destroy: synchronize");
+  std::lock_guard<std::mutex> lk(g_mu);
+  Mailbox& m = g_box[dev->id];
+  for (int p = 0; p < MK_MAX_PEERS; ++p) {
+    if (m.opened[p]) cudaIpcCloseMemHandle(m.peers[p]);
+    m.opened[p] = false;
+    m.peers[p] = nullptr;
+  }
+  if (m.local) cudaFree(m.local);
+  m = Mailbox();
+  return MK_OK;
+}

@@ -76,3 +76,54 @@ def barrier(group=None, device: torch.device | None = None) -> None:
             dist.barrier(group=group, device_ids=[device.index])
         else:
             dist.barrier(group=group)
+
+
+def exchange_bytes(mine: bytes, group=None) -> list[bytes]:
+    """All-gather one small byte string per rank (rank order)."""
+    rank, size = world(group)
+    if size == 1:
+        return [mine]
+    out: list = [None] * size
+    dist.all_gather_object(out, mine, group=group)
+    return list(out)
+
+
+class PeerReduce:
+    """Fused multi-GPU mapreduce: one launch per rank computes the local
+    reduction and exchanges the fp64 partial with every other rank through
+    CUDA-IPC-mapped peer memory (``mk_mapreduce_f32_allreduce``); no NCCL call
+    per reduction.  Create it collectively (every rank of ``group``, each on
+    its own GPU); every rank must then call ``__call__`` equally often."""
+
+    def __init__(self, group=None):
+        import ctypes as C
+
+        from . import _lib
+        self._lib = _lib
+        rank, size = world(group)
+        if size < 2:
+            raise ValueError("PeerReduce needs a process group of at least 2 ranks")
+        L = _lib.lib()
+        hs = L.mk_peer_handle_size()
+        buf = C.create_string_buffer(hs)
+        _lib.check(L.mk_peer_create(size, rank, buf), "mk_peer_create")
+        handles = exchange_bytes(buf.raw, group)
+        allh = C.create_string_buffer(b"".join(handles), hs * size)
+        _lib.check(L.mk_peer_connect(allh), "mk_peer_connect")
+        self.rank, self.size = rank, size
+
+    def __call__(self, x, f: str = "abs2", op: str = "add", init: float = 0.0,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+        """Global ``mapreduce(f, op, x)`` over all ranks' shards, as a
+        1-element fp64 device tensor on every rank (asynchronous)."""
+        from .array import current_stream_handle
+        L = self._lib.lib()
+        if out is None:
+            out = torch.empty(1, dtype=torch.float64, device=x.storage.device)
+        self._lib.check(L.mk_mapreduce_f32_allreduce(out.data_ptr(), x.pointer(), x.length,
+                                                     self._lib.MK_F[f], self._lib.MK_OP[op], float(init),
+                                                     current_stream_handle()), "mapreduce allreduce")
+        return out
+
+    def close(self) -> None:
+        self._lib.check(self._lib.lib().mk_peer_destroy(), "mk_peer_destroy")

@@ -192,6 +192,26 @@ MK_API int mk_matmul_tiled16_f32(float* C, const float* A, const float* B,
                           int64_t M, int64_t N, int64_t K,
                           int64_t lda, int64_t ldb, int64_t ldc, void* stream);
 
+/* ---- fused multi-GPU reduction (one process per GPU) ----------------------
+ * The reference is single-GPU; this is the exchange step of the sharded
+ * mapreduce.  Each rank creates a small peer mailbox on its device and gets
+ * its CUDA IPC handle (mk_peer_handle_size() bytes); the host exchanges the
+ * handles (e.g. an all-gather over the process group); every rank then maps
+ * the others' mailboxes with mk_peer_connect(all world handles, rank order).
+ * mk_mapreduce_f32_allreduce is mk_mapreduce_f32 whose last block also
+ * writes its fp64 partial into every rank's mailbox over NVLink and folds
+ * all ranks' partials in rank order (bounded wait; MK_ERR_TIMEOUT via
+ * mk_error_poll if a rank never arrives): every rank gets the same result,
+ * with no separate collective launch.  All ranks must call it the same number
+ * of times, on their own GPU.  mk_peer_destroy synchronises the device and
+ * releases the mailbox. */
+MK_API int mk_peer_handle_size(void);
+MK_API int mk_peer_create(int world, int rank, void* handle_out);
+MK_API int mk_peer_connect(const void* handles);
+MK_API int mk_peer_destroy(void);
+MK_API int mk_mapreduce_f32_allreduce(double* out_dev, const float* x, int64_t n,
+                                      int f, int op, double init, void* stream);
+
 /* ---- memory pools -------------------------------------------------------
  * Device memory from a per-device stream-ordered pool that keeps freed memory
  * cached (allocation and free are ordered on `stream`); replaces the CUDA.jl

@@ -66,3 +66,24 @@ def test_gloo_world2_combine():
     assert results["max"] == results["ref_max"]
     np.testing.assert_array_equal(results["counts"], results["ref_counts"])
     np.testing.assert_array_equal(results["wrap"], np.array([0xFFFFFFFE, 2], dtype=np.uint32))
+
+
+def _exchange_worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        got = distributed.exchange_bytes(bytes([rank]) * 64)
+        results[rank] = [bytes(g) for g in got]
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_handle_exchange_rank_order():
+    """The IPC-handle exchange of the fused multi-GPU reduction returns every
+    rank's bytes in rank order on every rank."""
+    mgr = mp.Manager()
+    results = mgr.dict()
+    mp.spawn(_exchange_worker, args=(2, _free_port(), results), nprocs=2, join=True)
+    for r in range(2):
+        assert results[r] == [bytes([0]) * 64, bytes([1]) * 64]

@@ -1,0 +1,61 @@
+"""Fused multi-GPU mapreduce over CUDA-IPC peer mailboxes
+(mk_mapreduce_f32_allreduce): two processes, one GPU each.  Needs >= 2 GPUs;
+with fewer it is skipped (the host logic is covered by the gloo tests)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import cutilecpu_b200 as mk
+    import oracle
+    from cutilecpu_b200 import distributed
+    try:
+        shards = [(np.random.Generator(np.random.Philox(100 + r)).random((1 << 22) + 17 * r, dtype=np.float32)
+                   * 2 - 1).astype(np.float32) for r in range(world)]
+        x = mk.MLIRArray(shards[rank])
+        pr = distributed.PeerReduce()
+        vals = []
+        for it in range(6):  # several epochs, alternating ops and parity slots
+            op = "add" if it % 2 == 0 else "max"
+            f = "abs2" if op == "add" else "identity"
+            init = 0.0 if op == "add" else -np.inf
+            vals.append(pr(x, f, op, init).item())
+        poll = mk._lib.lib().mk_error_poll(torch.cuda.current_stream().cuda_stream)
+        pr.close()
+        full = np.concatenate(shards)
+        results[rank] = {"vals": vals, "poll": poll, "sum": oracle.sum_sq(full), "max": float(full.max())}
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_fused_allreduce_two_gpus(cuda):
+    mgr = mp.Manager()
+    results = mgr.dict()
+    mp.spawn(_worker, args=(2, _port(), results), nprocs=2, join=True)
+    r0, r1 = results[0], results[1]
+    assert r0["poll"] == 0 and r1["poll"] == 0
+    assert r0["vals"] == r1["vals"]  # bit-identical on every rank
+    for it, v in enumerate(r0["vals"]):
+        if it % 2 == 0:
+            assert v == pytest.approx(r0["sum"], rel=1e-5)
+        else:
+            assert v == r0["max"]
