@@ -59,3 +59,39 @@ def test_fused_allreduce_two_gpus(cuda):
             assert v == pytest.approx(r0["sum"], rel=1e-5)
         else:
             assert v == r0["max"]
+
+
+def _timeout_worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["MK_WAIT_LIMIT_CYCLES"] = str(200_000_000)  # ~0.1 s: a short, bounded wait
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import cutilecpu_b200 as mk
+    from cutilecpu_b200 import distributed
+    try:
+        x = mk.MLIRArray(np.ones(1 << 20, dtype=np.float32))
+        pr = distributed.PeerReduce()
+        rc = 0
+        if rank == 0:  # rank 1 never joins this reduction: rank 0's wait must run out
+            v = pr(x).item()
+            rc = mk._lib.lib().mk_error_poll(torch.cuda.current_stream().cuda_stream)
+            results["v"] = v
+        dist.barrier()  # rank 1 keeps its mailbox mapped until rank 0 is done
+        pr.close()
+        results[rank] = rc
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_fused_allreduce_missing_rank_times_out(cuda):
+    """Failure detection without a GPU fault: a rank that does not arrive makes
+    the bounded in-kernel wait give up; the status is MK_ERR_TIMEOUT and the
+    GPU stays usable."""
+    mgr = mp.Manager()
+    results = mgr.dict()
+    mp.spawn(_timeout_worker, args=(2, _port(), results), nprocs=2, join=True)
+    from cutilecpu_b200 import _lib
+    assert results[0] == _lib.MK_ERR_TIMEOUT
+    assert results[1] == 0
