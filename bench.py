@@ -511,6 +511,7 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
     class Matmul(Workload):
         name = "matmul"
         metric = "matmul TFLOP/s (3xTF32 on tcgen05 tensor cores)"
+        launches_per_step = 3  # split_a, split_b, sgemm_tf32x3
         unit = "TFLOP/s"
         cfg = workloads.CONFIGS["matmul"]
 
@@ -711,6 +712,8 @@ PROFILED_TRAFFIC: dict[str, float | None] = {
     "gather": 15232078336 + 529049600,    # gather_f32_vec4, n = 2^27
     "histogram": 268520960 + 5512192,     # hist_smem, n = 2^26
     "matmul": 4584232704 + 257805056,     # sgemm_tf32x3, 8192^3 (split pre-pass excluded)
+    "scan": 1074146816 + 1024940032,      # scan_kernel (look-back), n = 2^28
+    "reduce_dims": 1073759232 + 2959872,  # seg_warp, 16384 x 16384, dims=1
 }
 
 
