@@ -717,7 +717,7 @@ def run_ours(kind: str, args, rank: int, world: int, local_rank: int) -> dict | 
 PROFILED_TRAFFIC: dict[str, float | None] = {
     "reduce": 1073769216 + 3054848,       # mapreduce_kernel<abs2,+>, n = 2^28
     "vadd": 8398336 + 0,                  # vadd_f32_vec4, n = 2^20 (stores stay in L2)
-    "gather": 15232078336 + 529049600,    # gather_f32_vec4, n = 2^27
+    "gather": 14957786368 + 536444160,    # gather_f32_vec4 (.cg loads), n = 2^27
     "histogram": 268520960 + 5512192,     # hist_smem, n = 2^26
     "matmul": 4584232704 + 257805056,     # sgemm_tf32x3, 8192^3 (split pre-pass excluded)
     "scan": 1074146816 + 1024940032,      # scan_kernel (look-back), n = 2^28
