@@ -226,6 +226,19 @@ def supports_atomics(backend) -> bool:
     return True
 
 
+def on_device(*arrays):
+    """Context in which a launch on ``arrays`` happens: their device made
+    current (the library launches on the current device and its current
+    stream), after checking that they all live on the same device."""
+    import contextlib
+    devs = {a.device for a in arrays if isinstance(a, MLIRArray)}
+    if len(devs) > 1:
+        raise _lib.MLIRKernelsError(f"MLIRCUDABackend: arguments live on different devices {sorted(devs)}")
+    if not devs or next(iter(devs)) == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(next(iter(devs)))
+
+
 def current_stream_handle() -> int:
     """cudaStream_t of torch's current stream (CUDA.jl's task-local stream)."""
     return torch.cuda.current_stream().cuda_stream

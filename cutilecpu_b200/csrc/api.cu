@@ -7,6 +7,7 @@
 // only: query the SM count, locate the error word, and hand out scratch.
 #include <stdlib.h>
 
+#include <atomic>
 #include <map>
 #include <tuple>
 #include <mutex>
@@ -24,6 +25,8 @@ static thread_local std::string t_last_error;
 static std::mutex g_mu;
 static constexpr int kMaxDevices = 64;
 static Device g_devices[kMaxDevices];
+// Set (release) once a device's state is complete; read (acquire) lock-free.
+static std::atomic<int> g_ready[kMaxDevices];
 static std::map<std::pair<int, cudaStream_t>, ReduceScratch> g_scratch;
 struct Workspace {
   void* ptr = nullptr;
@@ -64,6 +67,7 @@ static int init_device_locked(int id) {
     d.max_smem_optin = smem;
     d.err_word = static_cast<unsigned*>(word);
     d.id = id;
+    g_ready[id].store(1, std::memory_order_release);
   }
   if (prev != id) cudaSetDevice(prev);
   return rc;
@@ -80,7 +84,7 @@ Device* current_device() {
     fail(MK_ERR_INVALID, "device ordinal out of range");
     return nullptr;
   }
-  if (g_devices[id].id == id) return &g_devices[id];
+  if (g_ready[id].load(std::memory_order_acquire)) return &g_devices[id];
   std::lock_guard<std::mutex> lk(g_mu);
   if (init_device_locked(id) != MK_OK) return nullptr;
   return &g_devices[id];

@@ -29,7 +29,7 @@ import math
 from typing import Callable
 
 from . import _lib
-from .array import MLIRArray, MLIRCUDABackend, as_tuple, current_stream_handle
+from .array import MLIRArray, MLIRCUDABackend, as_tuple, current_stream_handle, on_device
 
 
 class KernelFunction:
@@ -99,18 +99,9 @@ class Kernel:
 
     def __call__(self, *args, ndrange=None, workgroupsize=None):
         nd, wg = self.launch_setup(ndrange, workgroupsize)
-        for a in args:
-            if isinstance(a, MLIRArray):
-                _same_device(args)
-                break
-        self.f.launcher(args, nd, wg, current_stream_handle())
+        with on_device(*args):
+            self.f.launcher(args, nd, wg, current_stream_handle())
         return None
-
-
-def _same_device(args) -> None:
-    devs = {a.device for a in args if isinstance(a, MLIRArray)}
-    if len(devs) > 1:
-        raise _lib.MLIRKernelsError(f"MLIRCUDABackend: arguments live on different devices {sorted(devs)}")
 
 
 def _need(a, name: str, eltypes: tuple[str, ...], min_len: int, what: str) -> MLIRArray:
@@ -195,7 +186,8 @@ def _launch_mm_naive(args, nd, wg, stream) -> None:
 def mul(Cm: MLIRArray, A: MLIRArray, B: MLIRArray) -> MLIRArray:
     """``LinearAlgebra.mul!(C, A, B)`` on MLIRArrays: C = A*B over all K terms
     on the tcgen05 tensor cores (3xTF32)."""
-    _launch_mm_naive((Cm, A, B), (A.size(1), B.size(2)), None, current_stream_handle())
+    with on_device(Cm, A, B):
+        _launch_mm_naive((Cm, A, B), (A.size(1), B.size(2)), None, current_stream_handle())
     return Cm
 
 

@@ -21,7 +21,7 @@ import operator
 import torch
 
 from . import _lib
-from .array import MLIRArray, current_stream_handle
+from .array import MLIRArray, current_stream_handle, on_device
 
 
 def identity(x):
@@ -91,9 +91,10 @@ def mapreduce_device(f, op, src, init=None, out: torch.Tensor | None = None) -> 
     init_v = _NEUTRAL[opname] if init is None else float(init)
     if out is None:
         out = torch.empty(1, dtype=torch.float64, device=src.storage.device)
-    _lib.check(_lib.lib().mk_mapreduce_f32(out.data_ptr(), src.pointer(), src.length,
-                                           _lib.MK_F[fname], _lib.MK_OP[opname], init_v,
-                                           current_stream_handle()), "mapreduce")
+    with on_device(src):
+        _lib.check(_lib.lib().mk_mapreduce_f32(out.data_ptr(), src.pointer(), src.length,
+                                               _lib.MK_F[fname], _lib.MK_OP[opname], init_v,
+                                               current_stream_handle()), "mapreduce")
     return out
 
 
@@ -112,9 +113,10 @@ def mapreduce_dims_into(f, op, R: MLIRArray, A, dim: int, init=None) -> MLIRArra
     if R.length != pre * post:
         raise _lib.MLIRKernelsError(f"mapreducedim!: result dims {R.dims} do not match reducing {A.dims} over {dim}")
     init_v = _NEUTRAL[opname] if init is None else float(init)
-    _lib.check(_lib.lib().mk_mapreduce_dim_f32(R.pointer(), A.pointer(), pre, ln, post, _lib.MK_F[fname],
-                                               _lib.MK_OP[opname], init_v, current_stream_handle()),
-               "mapreducedim!")
+    with on_device(R, A):
+        _lib.check(_lib.lib().mk_mapreduce_dim_f32(R.pointer(), A.pointer(), pre, ln, post, _lib.MK_F[fname],
+                                                   _lib.MK_OP[opname], init_v, current_stream_handle()),
+                   "mapreducedim!")
     return R
 
 
@@ -194,8 +196,10 @@ def accumulate(op, dst: MLIRArray, src: MLIRArray, init=None, inclusive: bool = 
         raise _lib.MLIRKernelsError("accumulate!: dst is shorter than src")
     opname = _op_name(op)
     init_v = _NEUTRAL[opname] if init is None else float(init)
-    _lib.check(_lib.lib().mk_accumulate_f32(dst.pointer(), src.pointer(), src.length, _lib.MK_OP[opname], init_v,
-                                            0 if inclusive else 1, current_stream_handle()), "accumulate!")
+    with on_device(dst, src):
+        _lib.check(_lib.lib().mk_accumulate_f32(dst.pointer(), src.pointer(), src.length, _lib.MK_OP[opname],
+                                                init_v, 0 if inclusive else 1, current_stream_handle()),
+                   "accumulate!")
     return dst
 
 

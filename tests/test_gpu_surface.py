@@ -120,3 +120,41 @@ def test_launch_errors_on_gpu(be):
         mk.vadd(be, 8)(c, mk.MLIRArray(np.ones(8, np.int32)), c, ndrange=8)
     with pytest.raises(mk.MLIRKernelsError, match="ndrange needs"):
         mk.vadd(be, 8)(c, c, c, ndrange=16)
+
+
+@pytest.mark.skipif(__import__("torch").cuda.device_count() < 2, reason="needs two GPUs")
+def test_launch_follows_the_arrays_device(be):
+    import torch
+    with torch.cuda.device(1):
+        a = mk.MLIRArray(np.arange(8, dtype=np.float32))
+        c = mk.zeros(be, "Float32", 8)
+    assert a.device == 1 and torch.cuda.current_device() == 0
+    mk.vadd(be, 8)(c, a, a, ndrange=8)  # launched on device 1, its current stream
+    assert mk.sum(a) == 28.0
+    np.testing.assert_array_equal(mk.Array(c), 2 * np.arange(8, dtype=np.float32))
+    with pytest.raises(mk.MLIRKernelsError, match="different devices"):
+        mk.vadd(be, 8)(c, a, mk.zeros(be, "Float32", 8), ndrange=8)
+
+
+def test_threads_share_the_library(be):
+    """Launches from several host threads (per-device state is created once,
+    scratch is per stream)."""
+    import threading
+    import torch
+    r = np.random.Generator(np.random.Philox(12))
+    xs = [r.random(1 << 20, dtype=np.float32) for _ in range(4)]
+    res = [None] * 4
+
+    def work(i):
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            x = mk.MLIRArray(xs[i])
+            res[i] = mk.sum(mk.abs2, x)
+
+    ts = [threading.Thread(target=work, args=(i,)) for i in range(4)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    for i in range(4):
+        assert res[i] == pytest.approx(oracle.sum_sq(xs[i]), rel=1e-5)
