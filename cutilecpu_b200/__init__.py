@@ -9,7 +9,8 @@ from ._lib import KernelException, MLIRKernelsError
 from .array import (Array, MLIRArray, MLIRCUDABackend, allocate, copyto, functional, get_backend,
                     launch_config, ones, supports_atomics, synchronize, zeros)
 from .kernels import Kernel, KernelFunction, gather, histogram, mm_naive, mm_tiled, mm_tiled_simt, mul, vadd
-from .reductions import (Broadcasted, abs2, accumulate, cumsum, count, identity, mapreduce, mapreducedim, maximum, minimum,
+from .reductions import (Broadcasted, abs2, accumulate, all_, any_, argmax, argmin, cumsum, extrema, findmax,
+                         findmin, count, identity, mapreduce, mapreducedim, maximum, minimum,
                      positive, prod, reduce, sum)
 from . import distributed, reductions
 from .pool import aligned_array, pointer_aligned, pool_allocate, pool_stats, pool_trim
@@ -18,7 +19,7 @@ __all__ = [
     "KernelException", "MLIRKernelsError", "Array", "MLIRArray", "MLIRCUDABackend", "allocate",
     "copyto", "functional", "get_backend", "launch_config", "ones", "supports_atomics", "synchronize",
     "zeros", "Kernel", "KernelFunction", "gather", "histogram", "mm_naive", "mm_tiled", "mm_tiled_simt", "mul", "vadd", "Broadcasted",
-    "abs2", "accumulate", "cumsum", "count", "identity", "mapreduce", "mapreducedim", "maximum", "minimum", "positive", "prod",
+    "abs2", "accumulate", "all_", "any_", "argmax", "argmin", "cumsum", "extrema", "findmax", "findmin", "count", "identity", "mapreduce", "mapreducedim", "maximum", "minimum", "positive", "prod",
     "reduce", "sum", "distributed", "aligned_array", "pointer_aligned", "pool_allocate", "pool_stats",
     "pool_trim",
 ]

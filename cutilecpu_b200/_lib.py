@@ -34,6 +34,7 @@ SIGNATURES = {
     "mk_mapreduce_f32_noalloc": (_int, [_vp, _vp, _i64, _int, _int, _f64, _vp]),
     "mk_mapreduce_dim_f32": (_int, [_vp, _vp, _i64, _i64, _i64, _int, _int, _f64, _vp]),
     "mk_accumulate_f32": (_int, [_vp, _vp, _i64, _int, _f64, _int, _vp]),
+    "mk_findext_f32": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
     "mk_gather_f32": (_int, [_vp, _vp, _i64, _vp, _i64, _vp]),
     "mk_hist_u32": (_int, [_vp, _i32, _vp, _i64, _vp]),
     "mk_hist": (_int, [_vp, _int, _i32, _vp, _int, _i64, _vp]),

@@ -208,3 +208,50 @@ def cumsum(src: MLIRArray) -> MLIRArray:
     from .array import MLIRCUDABackend, allocate
     dst = allocate(MLIRCUDABackend(), "Float32", src.dims)
     return accumulate(operator.add, dst, src)
+
+
+def _findext(src: MLIRArray, find_max: bool):
+    if not isinstance(src, MLIRArray) or src.eltype != "Float32":
+        raise _lib.MLIRKernelsError("findmax/findmin take a Float32 MLIRArray")
+    if src.length == 0:
+        raise ValueError("collection must be non-empty")
+    val = torch.empty(1, dtype=torch.float64, device=src.storage.device)
+    idx = torch.empty(1, dtype=torch.int64, device=src.storage.device)
+    with on_device(src):
+        _lib.check(_lib.lib().mk_findext_f32(val.data_ptr(), idx.data_ptr(), src.pointer(), src.length,
+                                             int(find_max), current_stream_handle()), "findmax")
+    return float(val.item()), int(idx.item())
+
+
+def findmax(src: MLIRArray):
+    """``findmax(x)``: (maximum, 1-based index of its first occurrence); NaN
+    counts as the maximum, as in Julia."""
+    return _findext(src, True)
+
+
+def findmin(src: MLIRArray):
+    """``findmin(x)``: (minimum, 1-based index); NaN counts as the minimum."""
+    return _findext(src, False)
+
+
+def argmax(src: MLIRArray) -> int:
+    return findmax(src)[1]
+
+
+def argmin(src: MLIRArray) -> int:
+    return findmin(src)[1]
+
+
+def extrema(src: MLIRArray):
+    """``extrema(x)`` = (minimum(x), maximum(x))."""
+    return minimum(src), maximum(src)
+
+
+def any_(pred, src) -> bool:
+    """``any(>(0), x)``."""
+    return count(pred, src) > 0
+
+
+def all_(pred, src) -> bool:
+    """``all(>(0), x)``."""
+    return count(pred, src) == src.length

@@ -132,6 +132,14 @@ MK_API int mk_mapreduce_dim_f32(float* out, const float* x, int64_t pre, int64_t
 MK_API int mk_accumulate_f32(float* out, const float* x, int64_t n, int op, double init, int exclusive,
                              void* stream);
 
+/* findmax (find_max != 0) or findmin of x[0, n), n >= 1: the extreme value
+ * (as fp64) and its 1-based index, written on the device.  Julia's rules: NaN
+ * counts as the maximum for findmax and as the minimum for findmin, +0.0 ranks
+ * above -0.0, the first index wins ties.  Replaces findmax/findmin/argmax/
+ * argmin on an MLIRArray (test/test_gpuarrays.jl:124-128). */
+MK_API int mk_findext_f32(double* val_out, int64_t* idx_out, const float* x, int64_t n, int find_max,
+                          void* stream);
+
 /* c[i] = a[idx1[i] - 1], i in [0, n); idx1 is 1-based into a[0, na).
  * Out-of-range indices write 0 and set the device error word.  Bit-exact.
  * Replaces a KA launch of `c[i] = a[idx[i]]` (indexing semantics

@@ -147,6 +147,22 @@ void or_accumulate_f64(double* out, const float* x, int64_t n, int op, double in
   }
 }
 
+/* findmax/findmin with Julia's rules (NaN counts as the extreme for both,
+ * +0.0 > -0.0, first index wins); returns the 1-based index. */
+int64_t or_findext_f32(double* val, const float* x, int64_t n, int find_max) {
+  int64_t best = 0;
+  for (int64_t i = 1; i < n; ++i) {
+    const float a = x[i], b = x[best];
+    int better;
+    if (a != a || b != b) better = (a != a) && !(b != b);
+    else if (a == b) better = (signbit(a) != signbit(b)) ? (find_max ? !signbit(a) : signbit(a)) : 0;
+    else better = find_max ? a > b : a < b;
+    if (better) best = i;
+  }
+  *val = (double)x[best];
+  return best + 1;
+}
+
 /* gather: c[i] = a[idx[i]], 1-based (src/lower.jl:4064-4077).  An index out of
  * [1, na] writes 0 and reports OR_ERR_DEVICE_FAULT (the reference raises a
  * BoundsError/KernelException without @inbounds). */

@@ -344,3 +344,48 @@ def test_hist_types_vs_oracle(L, bin_type, np_t, key_type, key_t, nbins):
     want = oracle.hist(keys[1:], nbins)[0].astype(np_t) + start
     np.testing.assert_array_equal(host(bd), want)
     assert poll(L) == _lib.MK_ERR_DEVICE_FAULT
+
+
+# ------------------------------------------------------- findmax/findmin -----
+
+def findext_dev(L, x_h, find_max, off=0):
+    xd = dev(np.concatenate([np.zeros(off, np.float32), x_h]))
+    v = torch.empty(1, dtype=torch.float64, device="cuda")
+    i = torch.empty(1, dtype=torch.int64, device="cuda")
+    assert L.mk_findext_f32(v.data_ptr(), i.data_ptr(), xd.data_ptr() + 4 * off, x_h.size, int(find_max),
+                            stream()) == 0, _lib.last_error()
+    return host(v)[0], int(host(i)[0])
+
+
+@pytest.mark.parametrize("n", [1, 3, 2000, 100_003, (1 << 24) + 1])
+@pytest.mark.parametrize("find_max", [True, False])
+@pytest.mark.parametrize("off", [0, 1])
+def test_findext_vs_oracle(L, n, find_max, off):
+    r = np.random.Generator(np.random.Philox(n))
+    x = r.random(n, dtype=np.float32)
+    x[n // 3] = x[n // 7] = x.max() if find_max else x.min()  # ties: the first index wins
+    gv, gi = findext_dev(L, x, find_max, off)
+    wv, wi = oracle.findext(x, find_max)
+    assert (gv, gi) == (wv, wi)
+
+
+def test_findext_nan_and_signed_zero(L):
+    x = np.float32([1, 5, np.nan, 5, np.nan])
+    assert findext_dev(L, x, True)[1] == 3 and findext_dev(L, x, False)[1] == 3
+    z = np.float32([-0.0, 0.0, -0.0, 0.0])
+    assert findext_dev(L, z, True)[1] == 2
+    assert findext_dev(L, np.float32([0.0, -0.0]), False)[1] == 2
+    assert L.mk_findext_f32(0, 0, 0, 0, 1, stream()) == _lib.MK_ERR_INVALID
+
+
+def test_findmax_surface(L):
+    import cutilecpu_b200 as mk
+    r = np.random.Generator(np.random.Philox(2000))
+    fx = r.random(2000, dtype=np.float32)
+    a = mk.MLIRArray(fx)
+    assert mk.findmax(a) == (float(fx.max()), int(np.argmax(fx)) + 1)
+    assert mk.findmin(a) == (float(fx.min()), int(np.argmin(fx)) + 1)
+    assert mk.argmax(a) == int(np.argmax(fx)) + 1 and mk.argmin(a) == int(np.argmin(fx)) + 1
+    assert mk.extrema(a) == (float(fx.min()), float(fx.max()))
+    s = mk.MLIRArray(fx - np.float32(0.5))
+    assert mk.any_(mk.positive, s) and not mk.all_(mk.positive, s)

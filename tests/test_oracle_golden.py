@@ -98,3 +98,16 @@ def test_matmul_properties_agree():
     np.testing.assert_allclose(oracle.matvec_chain_f64(A, B, v), C64 @ v, rtol=1e-10, atol=1e-9)
     ii = np.array([0, 63, 5]); jj = np.array([0, 79, 40])
     np.testing.assert_allclose(oracle.matmul_entries_f64(A, B, ii, jj), C64[ii, jj], rtol=1e-12)
+
+
+def test_findext_follows_julia_isless_rules():
+    # Base._rf_findmax keeps the current candidate unless isless(current, new);
+    # _rf_findmin uses isgreater, under which NaN is the smallest value.
+    x = np.float32([1, 3, 3, np.nan, 2, np.nan])
+    assert oracle.findext(x, True)[1] == 4 and oracle.findext(x, False)[1] == 4
+    z = np.float32([-0.0, 0.0, -0.0])
+    assert oracle.findext(z, True)[1] == 2      # +0.0 above -0.0
+    assert oracle.findext(np.float32([0.0, -0.0]), False)[1] == 2
+    r = np.random.Generator(np.random.Philox(2000)).random(2000, dtype=np.float32)
+    assert oracle.findext(r, True) == (float(r.max()), int(np.argmax(r)) + 1)
+    assert oracle.findext(r, False) == (float(r.min()), int(np.argmin(r)) + 1)
