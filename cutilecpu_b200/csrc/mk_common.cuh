@@ -47,7 +47,7 @@ int reduce_scratch(Device* d, cudaStream_t s, ReduceScratch* out);
 // that stage re-laid-out operands (the 3xTF32 GEMM's hi/lo panels) or keep
 // per-tile state (scan, dims reductions).  Grows with cudaMalloc (after a
 // cudaFree of the smaller buffer, once the stream has drained); never shrinks.
-enum : int { WS_GEMM = 0, WS_SCAN = 1, WS_DIMS = 2, WS_FIND = 3 };
+enum : int { WS_GEMM = 0, WS_SCAN = 1, WS_DIMS = 2, WS_FIND = 3, WS_GEMM_SPLIT = 4 };
 int stream_workspace(Device* d, cudaStream_t s, size_t bytes, void** out, int slot);
 
 // Bounded device waits give up after this many SM clock cycles (env

@@ -242,8 +242,8 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 
 __global__ void __launch_bounds__(kThreads, 1)
 sgemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-             float* __restrict__ C, int64_t M, int64_t N, int64_t ldc, int nkb, unsigned long long limit,
-             unsigned* __restrict__ err) {
+             float* __restrict__ C, int64_t M, int64_t N, int64_t ldc, int nkb_total, int kb_per_split, int tiles,
+             int64_t split_stride, unsigned long long limit, unsigned* __restrict__ err) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -255,10 +255,17 @@ sgemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Grouped raster: consecutive CTAs walk GROUP_M tile-rows column by column,
   // so a wave of ~148 CTAs shares ~16 A panels and ~9 B panels in L2.
+  // Split-K (small problems): CTA blockIdx.x handles tile (blockIdx.x % tiles)
+  // over k-blocks [split * kb_per_split, +kb_per_split) and writes its own
+  // partial C at C + split * split_stride (summed in order by split_reduce).
+  const int split = blockIdx.x / tiles;
+  const int kb0 = split * kb_per_split;
+  const int nkb = min(nkb_total - kb0, kb_per_split);
+  C += (int64_t)split * split_stride;
   int64_t m0, n0;
   {
     const int nM = (int)((M + BM - 1) / BM), nN = (int)((N + BN - 1) / BN);
-    const int t = blockIdx.x;
+    const int t = blockIdx.x % tiles;
     const int per_group = GROUP_M * nN;
     const int first_m = (t / per_group) * GROUP_M;
     const int gsize = min(GROUP_M, nM - first_m);
@@ -312,8 +319,8 @@ sgemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         }
         mbar_expect_tx(full0 + 8 * s, STAGE_BYTES);
         const uint32_t dst = smem0 + s * STAGE_BYTES;
-        tma_load_2d(dst, &tmA, kb * ROWF, (int)m0, full0 + 8 * s);
-        tma_load_2d(dst + A_STAGE, &tmB, kb * ROWF, (int)n0, full0 + 8 * s);
+        tma_load_2d(dst, &tmA, (kb0 + kb) * ROWF, (int)m0, full0 + 8 * s);
+        tma_load_2d(dst + A_STAGE, &tmB, (kb0 + kb) * ROWF, (int)n0, full0 + 8 * s);
         ++issued;
       }
       if (!ok) {
@@ -425,6 +432,19 @@ sgemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
   }
 }
 
+// Sum of the split-K partials in split order (deterministic): column-major
+// partials with leading dimension M, result into C with ldc.
+__global__ void __launch_bounds__(256) split_reduce(float* __restrict__ C, const float* __restrict__ P, int64_t M,
+                                                    int64_t N, int64_t ldc, int splits) {
+  const int64_t total = M * N, stride = (int64_t)gridDim.x * 256;
+  for (int64_t e = (int64_t)blockIdx.x * 256 + threadIdx.x; e < total; e += stride) {
+    float acc = __ldcs(P + e);
+    for (int sp = 1; sp < splits; ++sp) acc = __fadd_rn(acc, __ldcs(P + (int64_t)sp * total + e));
+    const int64_t j = e / M, i = e - j * M;
+    C[i + j * ldc] = acc;
+  }
+}
+
 // ------------------------------------------------------------- host --------
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -506,9 +526,34 @@ int sgemm_impl(const char* name, bool full_k, float* C, const float* A, const fl
   if ((rc = make_map(&mapB, B2, cols, (uint64_t)N, BN)) != MK_OK) return rc;
   if ((rc = mk::allow_dynamic_smem(reinterpret_cast<const void*>(sgemm_tf32x3), SMEM_BYTES)) != MK_OK) return rc;
   const int64_t tiles = mk::cdiv(N, BN) * mk::cdiv(M, BM);
-  dim3 grid((unsigned)tiles);
-  sgemm_tf32x3<<<grid, kThreads, SMEM_BYTES, s>>>(mapA, mapB, C, M, N, ldc, nkb, mk::wait_limit_cycles(),
-                                                   dev->err_word);
+  // Split K when the tiles cannot fill the GPU: each split keeps >= 1 chunk.
+  int splits = 1;
+  if (tiles < dev->sms) {
+    splits = (int)(dev->sms / tiles);
+    const int max_by_k = nkb / CHUNK_KB;
+    if (splits > max_by_k) splits = max_by_k;
+    if (splits > 8) splits = 8;
+    if (splits < 1) splits = 1;
+  }
+  const int kb_per_split = (int)mk::cdiv(nkb, splits);
+  splits = (int)mk::cdiv(nkb, kb_per_split);
+  float* target = C;
+  int64_t target_ld = ldc, split_stride = 0;
+  if (splits > 1) {
+    void* pw = nullptr;
+    if ((rc = mk::stream_workspace(dev, s, (size_t)splits * M * N * 4, &pw, mk::WS_GEMM_SPLIT)) != MK_OK) return rc;
+    target = static_cast<float*>(pw);
+    target_ld = M;
+    split_stride = M * N;
+  }
+  dim3 grid((unsigned)(tiles * splits));
+  sgemm_tf32x3<<<grid, kThreads, SMEM_BYTES, s>>>(mapA, mapB, target, M, N, target_ld, nkb, kb_per_split,
+                                                   (int)tiles, split_stride, mk::wait_limit_cycles(), dev->err_word);
+  if (splits > 1) {
+    int64_t blocks = mk::cdiv(M * N, 256);
+    if (blocks > (int64_t)dev->sms * 8) blocks = (int64_t)dev->sms * 8;
+    split_reduce<<<(unsigned)blocks, 256, 0, s>>>(C, target, M, N, ldc, splits);
+  }
   return mk::check_launch("mk_sgemm_3xtf32: launch");
 }
 
