@@ -164,7 +164,9 @@ MK_API int mk_hist_u32(uint32_t* counts, int32_t nbins, const int32_t* keys1, in
  * (examples/tiled_matmul.jl:34).  Replaces mm_tiled! launches
  * (examples/tiled_matmul.jl:28-48).  Row-major callers compute C^T = B^T A^T by
  * swapping operands.  Uses a per-stream device workspace of (M+N)*2*K*4 bytes
- * for the split operands (allocated on first use, grown as needed). */
+ * for the split operands, plus up to 8*M*N*4 bytes of split-K partials when
+ * the 128x256 tiles are fewer than the SMs (allocated on first use, grown as
+ * needed). */
 MK_API int mk_sgemm_3xtf32(float* C, const float* A, const float* B,
                            int64_t M, int64_t N, int64_t K,
                            int64_t lda, int64_t ldb, int64_t ldc, void* stream);
