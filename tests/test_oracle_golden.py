@@ -111,3 +111,23 @@ def test_findext_follows_julia_isless_rules():
     r = np.random.Generator(np.random.Philox(2000)).random(2000, dtype=np.float32)
     assert oracle.findext(r, True) == (float(r.max()), int(np.argmax(r)) + 1)
     assert oracle.findext(r, False) == (float(r.min()), int(np.argmin(r)) + 1)
+
+
+def test_dims_and_scan_oracles_agree_with_numpy():
+    # independent restatements (numpy fp64) of mapreducedim!(dims) and accumulate!
+    r = np.random.Generator(np.random.Philox(17))
+    m3 = np.asfortranarray(r.random((8, 4, 3), dtype=np.float32))
+    for d in (1, 2, 3):
+        np.testing.assert_allclose(oracle.mapreduce_dim(m3, d), m3.astype(np.float64).sum(d - 1, keepdims=True),
+                                   rtol=1e-13)
+        np.testing.assert_array_equal(oracle.mapreduce_dim(m3, d, "identity", "max", -np.inf),
+                                      m3.max(d - 1, keepdims=True).astype(np.float64))
+    x = r.random(1000, dtype=np.float32)
+    np.testing.assert_allclose(oracle.accumulate(x), np.cumsum(x.astype(np.float64)), rtol=1e-13)
+    ex = oracle.accumulate(x, "add", 1.5, exclusive=True)
+    assert ex[0] == 1.5
+    np.testing.assert_allclose(ex[1:], 1.5 + np.cumsum(x.astype(np.float64))[:-1], rtol=1e-13)
+    np.testing.assert_array_equal(oracle.accumulate(x, "max", -np.inf), np.maximum.accumulate(x).astype(np.float64))
+    # cumsum(1:1024) (test/test_downstream_ka.jl:39-42)
+    np.testing.assert_array_equal(oracle.accumulate(np.arange(1, 1025, dtype=np.float32)),
+                                  np.cumsum(np.arange(1, 1025)).astype(np.float64))
