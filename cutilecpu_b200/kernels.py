@@ -207,3 +207,32 @@ mm_naive = KernelFunction("mm_naive!", 2, _launch_mm_naive)
 mm_tiled = KernelFunction("mm_tiled!", 2, _launch_mm_tiled, static_wg=(16, 16))
 # The reference's 16x16 @localmem kernel run on CUDA cores (SIMT comparison point).
 mm_tiled_simt = KernelFunction("mm_tiled!", 2, _launch_mm_tiled_simt, static_wg=(16, 16))
+
+
+class Scale:
+    """The closure ``x -> a * x`` (a Float32 constant), for ``map_``."""
+
+    def __init__(self, a: float):
+        self.a = float(a)
+
+
+def axpby(dst: MLIRArray, a: float, x: MLIRArray, b: float = 0.0, y: MLIRArray | None = None) -> MLIRArray:
+    """``dst .= a .* x .+ b .* y`` (or ``a .* x`` without y), bit-exact with
+    Julia's Float32 evaluation order."""
+    n = x.length
+    _need(dst, "dst", ("Float32",), n, "axpby")
+    _need(x, "x", ("Float32",), n, "axpby")
+    if y is not None:
+        _need(y, "y", ("Float32",), n, "axpby")
+    with on_device(dst, x, y):
+        _lib.check(_lib.lib().mk_axpby_f32(dst.pointer(), a, x.pointer(), b, y.pointer() if y is not None else None,
+                                           n, current_stream_handle()), "axpby")
+    return dst
+
+
+def map_(f, dst: MLIRArray, src: MLIRArray) -> MLIRArray:
+    """``AK.map!(f, dst, src)`` for the closures this library implements:
+    ``Scale(a)`` (x -> a*x)."""
+    if isinstance(f, Scale):
+        return axpby(dst, f.a, src)
+    raise _lib.MLIRKernelsError(f"MLIRCUDABackend: map! has no kernel for {f!r} (supported: Scale(a))")

@@ -82,6 +82,13 @@ MK_API int mk_error_poll(void* stream);
  * examples/reflection_and_perf.jl:11-14) through ext/MLIRCUDAExt.jl:540-548. */
 MK_API int mk_vadd_f32(float* c, const float* a, const float* b, int64_t n, void* stream);
 
+/* out[i] = alpha*x[i] + beta*y[i] (y may be NULL: out[i] = alpha*x[i]),
+ * fp32 in Julia's order without FMA contraction, bit-exact.  Replaces
+ * AK.map!(x -> a*x, dst, src) and broadcasts like 2f0 .* a, a .+ b
+ * (test/test_downstream_ka.jl:18-20, test/test_gpuarrays.jl:31-32). */
+MK_API int mk_axpby_f32(float* out, float alpha, const float* x, float beta, const float* y, int64_t n,
+                        void* stream);
+
 /* out_dev[0] = op(init, op_{i<n} f(x[i])) as fp64, written on the device.
  * Sums/products accumulate in fp64 (per-thread fp32 groups of <= 8 terms);
  * max/min are exact.  Deterministic for a given device model.  n == 0 gives init.

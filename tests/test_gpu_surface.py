@@ -158,3 +158,24 @@ def test_threads_share_the_library(be):
         t.join()
     for i in range(4):
         assert res[i] == pytest.approx(oracle.sum_sq(xs[i]), rel=1e-5)
+
+
+def test_ak_map_and_broadcasts(be):
+    # AK.map!(x -> 2f0 * x, dst, src) (test/test_downstream_ka.jl:18-20);
+    # 2f0 .* a and a .+ b (test/test_gpuarrays.jl:31-32): bit-exact
+    r = np.random.Generator(np.random.Philox(31))
+    src_h, b_h = r.random(1027, dtype=np.float32), r.random(1027, dtype=np.float32)
+    src, b = mk.MLIRArray(src_h), mk.MLIRArray(b_h)
+    dst = mk.zeros(be, "Float32", 1027)
+    mk.map_(mk.Scale(2.0), dst, src)
+    np.testing.assert_array_equal(mk.Array(dst), np.float32(2) * src_h)
+    mk.axpby(dst, 1.0, src, 1.0, b)
+    np.testing.assert_array_equal(mk.Array(dst), src_h + b_h)
+    mk.axpby(dst, 3.0, src, -0.5, b)
+    np.testing.assert_array_equal(mk.Array(dst), np.float32(3) * src_h + np.float32(-0.5) * b_h)
+    v = src.view(2, 1001)  # misaligned view: scalar path
+    out = mk.zeros(be, "Float32", 1000)
+    mk.axpby(out, 2.0, v)
+    np.testing.assert_array_equal(mk.Array(out), np.float32(2) * src_h[1:1001])
+    with pytest.raises(mk.MLIRKernelsError, match="no kernel"):
+        mk.map_(lambda x: x + 1, dst, src)
