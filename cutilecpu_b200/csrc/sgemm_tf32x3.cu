@@ -31,6 +31,8 @@
 //                  internal fp32 accumulation is biased (it does not round to
 //                  nearest); bounding it to 256 terms keeps the K=8192 result
 //                  within 1e-5 of fp64.  Finally coalesced column-major stores.
+// sgemm_tf32x3_pair (below, the default) runs the same pipeline on CTA pairs
+// with 256x256 tiles; MK_SGEMM_PAIR=0 selects the one-CTA kernel.
 // Every mbarrier wait is bounded (mk::wait_limit_cycles); a timeout raises
 // ERRBIT_TIMEOUT in the device error word, stops the other roles, drains the
 // producer's in-flight copies (bounded), frees TMEM and returns.
@@ -432,6 +434,263 @@ sgemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
   }
 }
 
+// ---------------------------------------------------------- gemm, 2-SM ----
+//
+// The same product on CTA pairs (cluster of 2): one tcgen05.mma.cta_group::2
+// computes a 256x256 tile per pair.  Each CTA stages its own 128 rows of A2
+// and its own 128 rows of B2 (half the tile's N), so every SM reads 128+128
+// operand rows per k-step instead of 128+256: a third less shared-memory
+// traffic into the tensor core for the same FLOPs, and 6 pipeline stages fit.
+//   * both CTAs: TMA producer (warp 0) with .cta_group::2 loads that complete
+//     on the leader's (rank 0) full barrier; epilogue (warps 2-9) over its own
+//     128 TMEM lanes; TMEM is allocated and freed by warp 2 of both CTAs;
+//   * leader only: the MMA issuer; its commits arrive on both CTAs' barriers
+//     (tcgen05.commit multicast), and it waits on its accumulator-empty
+//     barrier, which both CTAs' epilogue warps arrive on.
+// Loads carry no cluster multicast: every CTA loads only its own tiles.
+
+constexpr int P_BM = 128;                     // A rows per CTA (pair tile M = 256)
+constexpr int P_BNH = 128;                    // B rows per CTA (pair tile N = 256)
+constexpr int P_STAGES = 6;
+constexpr int P_A_STAGE = P_BM * ROWF * 4;    // 16 KiB
+constexpr int P_B_STAGE = P_BNH * ROWF * 4;   // 16 KiB
+constexpr int P_STAGE_BYTES = P_A_STAGE + P_B_STAGE;
+constexpr int P_GROUP_M = 8;                  // pair tile-rows per raster group
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+// kind::tf32, D f32, A/B tf32 K-major, M=256 (pair), N=256.
+constexpr uint32_t P_IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(256 >> 3) << 17) |
+                             ((uint32_t)(256 >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the same offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n barrier.cluster.wait.acquire;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(bar_cluster)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(P_IDESC), "r"(acc)
+      : "memory");
+}
+
+// Arrive on the barrier at offset `bar` in both CTAs of the pair once every
+// previously issued tcgen05 operation of this thread has completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+sgemm_tf32x3_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                  float* __restrict__ C, int64_t M, int64_t N, int64_t ldc, int nkb_total, int kb_per_split,
+                  int tiles, int64_t split_stride, unsigned long long limit, unsigned* __restrict__ err) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE_BYTES);
+  // bars: [0,S) full (leader), [S,2S) empty, 2S+{0,1} acc_full, 2S+{2,3} acc_empty (leader), 2S+4 done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * P_STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int split = pair / tiles;
+  const int kb0 = split * kb_per_split;
+  const int nkb = min(nkb_total - kb0, kb_per_split);
+  C += (int64_t)split * split_stride;
+  int64_t m0, n0;  // the pair's tile origin
+  {
+    const int nM = (int)((M + 255) / 256), nN = (int)((N + 255) / 256);
+    const int t = pair % tiles;
+    const int per_group = P_GROUP_M * nN;
+    const int first_m = (t / per_group) * P_GROUP_M;
+    const int gsize = min(P_GROUP_M, nM - first_m);
+    const int r = t % per_group;
+    m0 = (int64_t)(first_m + r % gsize) * 256;
+    n0 = (int64_t)(r / gsize) * 256;
+  }
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + P_STAGES);
+  const uint32_t accf0 = smem_u32(bars + 2 * P_STAGES), acce0 = smem_u32(bars + 2 * P_STAGES + 2);
+  const uint32_t done = smem_u32(bars + 2 * P_STAGES + 4);
+  const int nchunks = (nkb + CHUNK_KB - 1) / CHUNK_KB;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf0 + 8 * b, 1);
+      mbar_init(acce0 + 8 * b, 2 * EPI_WARPS);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer (both CTAs): own A rows and own half of the B rows
+      const uint32_t smem0 = smem_u32(smem);
+      const int a_row = (int)(m0 + rank * P_BM), b_row = (int)(n0 + rank * P_BNH);
+      bool ok = true;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % P_STAGES;
+        if (kb >= P_STAGES && !wait_bounded(empty0 + 8 * s, ((kb / P_STAGES) - 1) & 1, limit, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (leader) mbar_expect_tx(full0 + 8 * s, 2 * P_STAGE_BYTES);
+        const uint32_t bar = map_rank(full0 + 8 * s, 0);
+        const uint32_t dst = smem0 + s * P_STAGE_BYTES;
+        tma_load_2d_pair(dst, &tmA, (kb0 + kb) * ROWF, a_row, bar);
+        tma_load_2d_pair(dst + P_A_STAGE, &tmB, (kb0 + kb) * ROWF, b_row, bar);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(err, mk::ERRBIT_TIMEOUT);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---- MMA issuer (leader): chunk c accumulates afresh into TMEM buffer c & 1
+      const uint32_t smem0 = smem_u32(smem);
+      bool ok = true;
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int b = c & 1;
+        if (c >= 2 && !wait_bounded(acce0 + 8 * b, ((c >> 1) - 1) & 1, limit, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(b * BN);
+        const int kb_end = min(nkb, (c + 1) * CHUNK_KB);
+        for (int kb = c * CHUNK_KB; kb < kb_end; ++kb) {
+          const int s = kb % P_STAGES;
+          if (!wait_bounded(full0 + 8 * s, (kb / P_STAGES) & 1, limit, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem0 + s * P_STAGE_BYTES, bb = a + P_A_STAGE;
+          mma_tf32_pair(d, smem_desc(a + 0), smem_desc(bb + 0), kb > c * CHUNK_KB ? 1u : 0u);
+          mma_tf32_pair(d, smem_desc(a + 32), smem_desc(bb + 32), 1u);
+          mma_tf32_pair(d, smem_desc(a + 0), smem_desc(bb + 64), 1u);
+          mma_tf32_pair(d, smem_desc(a + 32), smem_desc(bb + 96), 1u);
+          mma_tf32_pair(d, smem_desc(a + 64), smem_desc(bb + 0), 1u);
+          mma_tf32_pair(d, smem_desc(a + 96), smem_desc(bb + 32), 1u);
+          mma_commit_pair(empty0 + 8 * s);
+        }
+        if (ok) mma_commit_pair(accf0 + 8 * b);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(err, mk::ERRBIT_TIMEOUT);
+      }
+      mma_commit_pair(done);
+    }
+  } else {
+    // ---- epilogue (both CTAs): 8 warps over this CTA's 128 TMEM lanes x 256 columns
+    const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
+    float acc[BN / 2];
+#pragma unroll
+    for (int j = 0; j < BN / 2; ++j) acc[j] = 0.0f;
+    bool ok = true;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    for (int c = 0; c < nchunks; ++c) {
+      const int b = c & 1;
+      bool w = wait_bounded(accf0 + 8 * b, (c >> 1) & 1, limit, abort_flag);
+      w = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
+      if (!w) {
+        ok = false;
+        if (lane == 0) *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t t0 = tmem + lane_base + (uint32_t)(b * BN + h * (BN / 2));
+#pragma unroll
+      for (int i = 0; i < BN / 64; ++i) {
+        uint32_t r[32];
+        tmem_ld32(t0 + i * 32, r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[i * 32 + j] = __fadd_rn(acc[i * 32 + j], __uint_as_float(r[j]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(map_rank(acce0 + 8 * b, 0));
+    }
+    if (ok) {
+      const int64_t row = m0 + rank * P_BM + q * 32 + lane;
+      if (row < M) {
+        const int64_t nb = n0 + h * (BN / 2);
+        float* dst = C + row + nb * ldc;
+#pragma unroll
+        for (int j = 0; j < BN / 2; ++j)
+          if (nb + j < N) __stcs(dst + (int64_t)j * ldc, acc[j]);
+      }
+    } else {
+      atomicOr(err, mk::ERRBIT_TIMEOUT);
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();  // every role of both CTAs has finished with the peer's barriers and TMEM
+  if (warp == 2) {
+    volatile int no_abort = 0;
+    wait_bounded(done, 0, limit, &no_abort);  // every MMA writing this CTA's TMEM has completed
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+  __syncwarp();
+  cluster_sync_all();
+}
+
 // Sum of the split-K partials in split order (deterministic): column-major
 // partials with leading dimension M, result into C with ldc.
 __global__ void __launch_bounds__(256) split_reduce(float* __restrict__ C, const float* __restrict__ P, int64_t M,
@@ -479,6 +738,15 @@ int make_map(CUtensorMap* map, const float* base, uint64_t cols, uint64_t rows, 
 
 namespace {
 
+// MK_SGEMM_PAIR=0 selects the one-CTA kernel (128x256 tiles); default: CTA pairs.
+bool use_pair_kernel() {
+  static const bool on = [] {
+    const char* e = getenv("MK_SGEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 // full_k: every K term (LinearAlgebra.mul!); otherwise 16*floor(K/16) terms
 // (mm_tiled!).  The remainder of a full-K product is zero-padded by the split.
 int sgemm_impl(const char* name, bool full_k, float* C, const float* A, const float* B, int64_t M, int64_t N,
@@ -521,15 +789,20 @@ int sgemm_impl(const char* name, bool full_k, float* C, const float* A, const fl
     else
       split_b<false><<<(unsigned)blocks, 256, 0, s>>>(B2, B, N, ldb, nkb, kvalid);
   }
+  const bool pair = use_pair_kernel();
   CUtensorMap mapA, mapB;
   if ((rc = make_map(&mapA, A2, cols, (uint64_t)M, BM)) != MK_OK) return rc;
-  if ((rc = make_map(&mapB, B2, cols, (uint64_t)N, BN)) != MK_OK) return rc;
-  if ((rc = mk::allow_dynamic_smem(reinterpret_cast<const void*>(sgemm_tf32x3), SMEM_BYTES)) != MK_OK) return rc;
-  const int64_t tiles = mk::cdiv(N, BN) * mk::cdiv(M, BM);
+  if ((rc = make_map(&mapB, B2, cols, (uint64_t)N, pair ? P_BNH : BN)) != MK_OK) return rc;
+  const void* kfn = pair ? reinterpret_cast<const void*>(sgemm_tf32x3_pair) : reinterpret_cast<const void*>(sgemm_tf32x3);
+  const int smem_bytes = pair ? P_SMEM_BYTES : SMEM_BYTES;
+  if ((rc = mk::allow_dynamic_smem(kfn, smem_bytes)) != MK_OK) return rc;
+  // tiles of C: 128x256 per CTA, or 256x256 per CTA pair
+  const int64_t tiles = pair ? mk::cdiv(N, 256) * mk::cdiv(M, 256) : mk::cdiv(N, BN) * mk::cdiv(M, BM);
+  const int64_t slots = pair ? dev->sms / 2 : dev->sms;  // tiles that run at once
   // Split K when the tiles cannot fill the GPU: each split keeps >= 1 chunk.
   int splits = 1;
-  if (tiles < dev->sms) {
-    splits = (int)(dev->sms / tiles);
+  if (tiles < slots) {
+    splits = (int)(slots / tiles);
     const int max_by_k = nkb / CHUNK_KB;
     if (splits > max_by_k) splits = max_by_k;
     if (splits > 8) splits = 8;
@@ -546,9 +819,16 @@ int sgemm_impl(const char* name, bool full_k, float* C, const float* A, const fl
     target_ld = M;
     split_stride = M * N;
   }
-  dim3 grid((unsigned)(tiles * splits));
-  sgemm_tf32x3<<<grid, kThreads, SMEM_BYTES, s>>>(mapA, mapB, target, M, N, target_ld, nkb, kb_per_split,
-                                                   (int)tiles, split_stride, mk::wait_limit_cycles(), dev->err_word);
+  if (pair) {
+    dim3 grid((unsigned)(2 * tiles * splits));
+    sgemm_tf32x3_pair<<<grid, kThreads, P_SMEM_BYTES, s>>>(mapA, mapB, target, M, N, target_ld, nkb, kb_per_split,
+                                                           (int)tiles, split_stride, mk::wait_limit_cycles(),
+                                                           dev->err_word);
+  } else {
+    dim3 grid((unsigned)(tiles * splits));
+    sgemm_tf32x3<<<grid, kThreads, SMEM_BYTES, s>>>(mapA, mapB, target, M, N, target_ld, nkb, kb_per_split,
+                                                     (int)tiles, split_stride, mk::wait_limit_cycles(), dev->err_word);
+  }
   if (splits > 1) {
     int64_t blocks = mk::cdiv(M * N, 256);
     if (blocks > (int64_t)dev->sms * 8) blocks = (int64_t)dev->sms * 8;
