@@ -13,6 +13,8 @@
 #include <mutex>
 #include <utility>
 
+#include <cudaTypedefs.h>
+
 #include "mk_common.cuh"
 
 // One error word per device: every module global exists once per device
@@ -162,6 +164,29 @@ unsigned long long wait_limit_cycles() {
     return x ? x : (1ull << 32);
   }();
   return v;
+}
+
+int encode_rows_f32(CUtensorMap* map, const float* base, uint64_t cols, uint64_t rows, uint32_t box_cols,
+                    uint32_t box_rows, const char* who) {
+  using Fn = PFN_cuTensorMapEncodeTiled_v12000;
+  static Fn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<Fn>(p);
+  }();
+  if (!fn) return fail(MK_ERR_CUDA, std::string(who) + ": cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 4};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MK_ERR_CUDA, std::string(who) + ": cuTensorMapEncodeTiled failed");
+  return MK_OK;
 }
 
 }  // namespace mk

@@ -2,6 +2,7 @@
 // reporting, per-device state, launch-geometry helpers.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string>
@@ -56,6 +57,12 @@ unsigned long long wait_limit_cycles();
 
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (device, kernel).
 int allow_dynamic_smem(const void* kernel, size_t bytes);
+
+// Tensor map of a row-major (rows x cols) fp32 array for 2-D TMA copies of
+// box_rows x box_cols boxes with 128-byte swizzle (box_cols * 4 <= 128).
+// base must be 16-byte aligned and cols a multiple of 4.
+int encode_rows_f32(CUtensorMap* map, const float* base, uint64_t cols, uint64_t rows, uint32_t box_cols,
+                    uint32_t box_rows, const char* who);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

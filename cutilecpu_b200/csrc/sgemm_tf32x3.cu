@@ -43,6 +43,7 @@
 #include <mutex>
 #include <string>
 
+#include "mbarrier.cuh"
 #include "mk_common.cuh"
 
 #ifndef MK_SGEMM_CHUNK_KB
@@ -50,6 +51,8 @@
 #endif
 
 namespace {
+
+using namespace mk::tma;
 
 constexpr int BM = 128;
 constexpr int BN = 256;
@@ -71,51 +74,6 @@ constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >
                            ((uint32_t)(BM >> 4) << 24);
 
 // ---------------------------------------------------------------- PTX ------
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Wait for phase `parity` of `bar` to complete; false on timeout or when
-// another role raised the abort flag.
-__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, unsigned long long limit,
-                                             volatile int* abort_flag) {
-  const long long t0 = clock64();
-  uint32_t spins = 0;
-  while (!mbar_try_wait(bar, parity)) {
-    if ((++spins & 63u) == 0) {
-      if (*abort_flag) return false;
-      if ((unsigned long long)(clock64() - t0) > limit) return false;
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          dst),
-      "l"(map), "r"(c0), "r"(c1), "r"(bar)
-      : "memory");
-}
 
 // Shared-memory matrix descriptor: K-major, 128B swizzle, 8-row groups 1024 B apart.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
@@ -237,10 +195,6 @@ __global__ void __launch_bounds__(256) split_b(float* __restrict__ B2, const flo
 }
 
 // -------------------------------------------------------------- gemm -------
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
 
 __global__ void __launch_bounds__(kThreads, 1)
 sgemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -706,33 +660,10 @@ __global__ void __launch_bounds__(256) split_reduce(float* __restrict__ C, const
 
 // ------------------------------------------------------------- host --------
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      p = nullptr;
-    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }();
-  return fn;
-}
-
 // Row-major (rows x cols) fp32 panel, boxes of box_rows x 32 with 128B swizzle.
 int make_map(CUtensorMap* map, const float* base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
-  auto enc = encode_fn();
-  if (!enc) return mk::fail(MK_ERR_CUDA, "mk_sgemm_3xtf32: cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols * 4};
-  cuuint32_t box[2] = {(cuuint32_t)ROWF, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return mk::fail(MK_ERR_CUDA, "mk_sgemm_3xtf32: cuTensorMapEncodeTiled failed");
-  return MK_OK;
+  return mk::encode_rows_f32(map, base, cols, rows, (uint32_t)ROWF, box_rows, "mk_sgemm_3xtf32");
 }
-
 
 }  // namespace
 

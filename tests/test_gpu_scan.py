@@ -36,7 +36,10 @@ def test_cumsum_1_to_1024(cuda):
     np.testing.assert_array_equal(scan(x), np.cumsum(np.arange(1, 1025)).astype(np.float32))
 
 
-@pytest.mark.parametrize("n", [1, 2, 31, 4095, 4096, 4097, 100_000, (1 << 22) + 7, 1 << 26])
+# 8192: one 256-row tile; 8197: a second tile holding only the partial row;
+# 3*8192 + 233: ragged last tile with a partial row
+@pytest.mark.parametrize("n", [1, 2, 31, 4095, 4096, 4097, 8192, 8197, 3 * 8192 + 233, 100_000, (1 << 22) + 7,
+                               1 << 26])
 @pytest.mark.parametrize("exclusive", [False, True])
 def test_scan_add_sizes(cuda, n, exclusive):
     r = np.random.Generator(np.random.Philox(n))
@@ -49,6 +52,21 @@ def test_scan_max_min_exact(cuda, op, init):
     r = np.random.Generator(np.random.Philox(7))
     x = r.standard_normal(300_001, dtype=np.float32)
     np.testing.assert_array_equal(scan(x, op, init), oracle.accumulate(x, op, init).astype(np.float32))
+
+
+@pytest.mark.parametrize("n", [8197, 300_001])
+def test_scan_mul_exact(cuda, n):
+    r = np.random.Generator(np.random.Philox(10))
+    x = np.where(r.random(n) < 0.5, -1.0, 1.0).astype(np.float32)  # products stay exactly +-1
+    for exclusive in (False, True):
+        np.testing.assert_array_equal(scan(x, "mul", 1.0, exclusive),
+                                      oracle.accumulate(x, "mul", 1.0, exclusive).astype(np.float32))
+
+
+def test_scan_inplace_exclusive_ragged(cuda):
+    r = np.random.Generator(np.random.Philox(11))
+    x = r.random((1 << 20) + 29, dtype=np.float32)
+    check_add(scan(x, inplace=True, exclusive=True, init=2.0), x, 2.0, True)
 
 
 def test_scan_misaligned_and_inplace(cuda):
