@@ -8,8 +8,10 @@
 // Two shapes of parallelism, both accumulating in fp64 (max/min exact) and
 // rounding once to Float32:
 //   * pre == 1 (dims=1): each output is a contiguous segment; a warp (or, for
-//     few long segments, a 256-thread block) strides it with coalesced loads;
-//   * pre > 1: one thread per p walks k with loads coalesced across p.  When
+//     few long segments, a 256-thread block) strides it with coalesced 16-byte
+//     loads, four in flight per thread;
+//   * pre > 1: one thread per p walks k with loads coalesced across p, four
+//     k-steps in flight.  When
 //     pre*post threads cannot fill the GPU, k is cut into chunks whose fp64
 //     partials go to a per-stream workspace and are folded in chunk order by
 //     a second launch, so results stay deterministic.
@@ -32,6 +34,39 @@ __device__ __forceinline__ double warp_reduce(double v) {
   return v;
 }
 
+// Fold of one contiguous segment by `nt` cooperating threads (index i): the
+// scalar head up to the first 16-byte boundary, then float4 vectors with four
+// in flight per thread into four accumulators (a fixed order, so the result
+// is deterministic), then the scalar tail.  Returns this thread's partial.
+template <int F, int OP>
+__device__ __forceinline__ double fold_segment(const float* __restrict__ seg, int64_t len, int i, int nt) {
+  double a0 = neutral<OP>(), a1 = neutral<OP>(), a2 = neutral<OP>(), a3 = neutral<OP>();
+  int64_t h = (int64_t)(((16u - (reinterpret_cast<uintptr_t>(seg) & 15u)) & 15u) / 4u);
+  if (h > len) h = len;
+  if (i < h) a0 = fold<F, OP>(a0, __ldcs(seg + i));
+  const float4* v = reinterpret_cast<const float4*>(seg + h);
+  const int64_t n4 = (len - h) / 4;
+  auto fold4 = [](double a, float4 q) {
+    a = fold<F, OP>(a, q.x);
+    a = fold<F, OP>(a, q.y);
+    a = fold<F, OP>(a, q.z);
+    return fold<F, OP>(a, q.w);
+  };
+  int64_t j = i;
+  for (; j + 3 * nt < n4; j += 4 * nt) {
+    const float4 q0 = __ldcs(v + j), q1 = __ldcs(v + j + nt), q2 = __ldcs(v + j + 2 * nt),
+                 q3 = __ldcs(v + j + 3 * nt);
+    a0 = fold4(a0, q0);
+    a1 = fold4(a1, q1);
+    a2 = fold4(a2, q2);
+    a3 = fold4(a3, q3);
+  }
+  for (; j < n4; j += nt) a0 = fold4(a0, __ldcs(v + j));
+  const int64_t tail = h + 4 * n4;
+  for (int64_t k = tail + i; k < len; k += nt) a1 = fold<F, OP>(a1, __ldcs(seg + k));
+  return combine<OP>(combine<OP>(a0, a1), combine<OP>(a2, a3));
+}
+
 // pre == 1, a warp per segment.
 template <int F, int OP>
 __global__ void __launch_bounds__(256) seg_warp(float* __restrict__ out, const float* __restrict__ x, int64_t len,
@@ -39,9 +74,7 @@ __global__ void __launch_bounds__(256) seg_warp(float* __restrict__ out, const f
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * 8;
   for (int64_t q = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); q < post; q += warps) {
-    const float* seg = x + q * len;
-    double acc = neutral<OP>();
-    for (int64_t k = lane; k < len; k += 32) acc = fold<F, OP>(acc, __ldcs(seg + k));
+    double acc = fold_segment<F, OP>(x + q * len, len, lane, 32);
     acc = warp_reduce<OP>(acc);
     if (lane == 0) out[q] = (float)combine<OP>(init, acc);
   }
@@ -53,9 +86,7 @@ __global__ void __launch_bounds__(256) seg_block(float* __restrict__ out, const 
                                                  int64_t post, double init) {
   __shared__ double sm[8];
   for (int64_t q = blockIdx.x; q < post; q += gridDim.x) {
-    const float* seg = x + q * len;
-    double acc = neutral<OP>();
-    for (int64_t k = threadIdx.x; k < len; k += 256) acc = fold<F, OP>(acc, __ldcs(seg + k));
+    double acc = fold_segment<F, OP>(x + q * len, len, threadIdx.x, 256);
     acc = warp_reduce<OP>(acc);
     if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = acc;
     __syncthreads();
@@ -81,8 +112,19 @@ __global__ void __launch_bounds__(256) strided(float* __restrict__ out, double* 
   for (int64_t o = (int64_t)blockIdx.x * 256 + threadIdx.x; o < total; o += stride) {
     const int64_t q = o / pre, p = o - q * pre;
     const float* base = x + p + q * pre * len;
-    double acc = neutral<OP>();
-    for (int64_t k = k0; k < k1; ++k) acc = fold<F, OP>(acc, __ldcs(base + k * pre));
+    // four independent k-chains (k mod 4), combined in a fixed order
+    double a0 = neutral<OP>(), a1 = neutral<OP>(), a2 = neutral<OP>(), a3 = neutral<OP>();
+    int64_t k = k0;
+    for (; k + 3 < k1; k += 4) {
+      const float v0 = __ldcs(base + k * pre), v1 = __ldcs(base + (k + 1) * pre), v2 = __ldcs(base + (k + 2) * pre),
+                  v3 = __ldcs(base + (k + 3) * pre);
+      a0 = fold<F, OP>(a0, v0);
+      a1 = fold<F, OP>(a1, v1);
+      a2 = fold<F, OP>(a2, v2);
+      a3 = fold<F, OP>(a3, v3);
+    }
+    for (; k < k1; ++k) a0 = fold<F, OP>(a0, __ldcs(base + k * pre));
+    const double acc = combine<OP>(combine<OP>(a0, a1), combine<OP>(a2, a3));
     if (gridDim.y == 1) out[o] = (float)combine<OP>(init, acc);
     else partial[(int64_t)blockIdx.y * total + o] = acc;
   }

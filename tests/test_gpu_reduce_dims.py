@@ -37,7 +37,7 @@ def check(got, want, exact):
 
 
 @pytest.mark.parametrize("shape", [(32, 17), (8, 4, 3), (1, 5), (5, 1), (4096, 300), (300, 4096),
-                                   (1 << 22, 2), (2, 1 << 22), (7, 100_003, 3)])
+                                   (1 << 22, 2), (2, 1 << 22), (7, 100_003, 3), (4097, 33), (1023, 257)])
 @pytest.mark.parametrize("f,op,init", [("identity", "add", 0.0), ("abs2", "add", 0.0),
                                        ("identity", "max", -np.inf), ("identity", "min", np.inf)])
 def test_dims_vs_oracle(cuda, shape, f, op, init):
