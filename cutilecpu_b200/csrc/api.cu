@@ -105,11 +105,13 @@ int reduce_scratch(Device* d, cudaStream_t s, ReduceScratch* out) {
   size_t bytes = sizeof(double) * kMaxReduceBlocks + 256;
   cudaError_t e = cudaMalloc(&p, bytes);
   if (e != cudaSuccess) return fail_cuda(e, "cudaMalloc(reduce scratch)");
-  // The ticket starts at zero; every reduction leaves it at zero again.
-  e = cudaMemset(p, 0, bytes);
+  // The ticket starts at zero; every reduction leaves it at zero again.  The
+  // zeroing is ordered on `s` itself: a plain cudaMemset runs on the legacy
+  // default stream, which does not order a non-blocking stream's next kernel.
+  e = cudaMemsetAsync(p, 0, bytes, s);
   if (e != cudaSuccess) {
     cudaFree(p);
-    return fail_cuda(e, "cudaMemset(reduce scratch)");
+    return fail_cuda(e, "cudaMemsetAsync(reduce scratch)");
   }
   ReduceScratch rs;
   rs.partials = static_cast<double*>(p);

@@ -125,6 +125,7 @@ mapreduce_kernel(const float* __restrict__ x, int64_t n, int head, double init,
 
   const float4* x4 = reinterpret_cast<const float4*>(x + head);
   const int64_t n4 = (n - head) / 4;
+  float ext[4] = {neutral32<OP>(), neutral32<OP>(), neutral32<OP>(), neutral32<OP>()};
   int64_t i = tid;
   for (; i + (kUnroll - 1) * stride < n4; i += kUnroll * stride) {
     float4 v[kUnroll];
@@ -139,11 +140,22 @@ mapreduce_kernel(const float* __restrict__ x, int64_t n, int head, double init,
                    (mapf(F, v[u + 1].z) + mapf(F, v[u + 1].w));
         acc += (double)(g0 + g1);
       }
+    } else if (OP == MK_OP_MAX || OP == MK_OP_MIN) {
+      // max/min are exact: fold in fp32, one independent chain per vector lane
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        ext[0] = combine32<OP>(ext[0], mapf(F, v[u].x));
+        ext[1] = combine32<OP>(ext[1], mapf(F, v[u].y));
+        ext[2] = combine32<OP>(ext[2], mapf(F, v[u].z));
+        ext[3] = combine32<OP>(ext[3], mapf(F, v[u].w));
+      }
     } else {
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) fold4<F, OP>(acc, v[u]);
     }
   }
+  if (OP == MK_OP_MAX || OP == MK_OP_MIN)
+    acc = combine<OP>(acc, (double)combine32<OP>(combine32<OP>(ext[0], ext[1]), combine32<OP>(ext[2], ext[3])));
   for (; i < n4; i += stride) fold4<F, OP>(acc, __ldcs(x4 + i));
   // Scalar head (before the first 16-byte boundary) and tail (< 4 elements).
   const int64_t tail_start = head + n4 * 4;

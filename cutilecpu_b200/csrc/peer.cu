@@ -57,7 +57,9 @@ extern "C" int mk_peer_create(int world, int rank, void* handle_out) {
   Mailbox& m = g_box[dev->id];
   if (m.local) return mk::fail(MK_ERR_INVALID, "mk_peer_create: mailbox already exists (mk_peer_destroy first)");
   cudaError_t e = cudaMalloc(&m.local, mk::kMailboxBytes);
+  // zeroed and complete before any stream (blocking or not) can use it
   if (e == cudaSuccess) e = cudaMemset(m.local, 0, mk::kMailboxBytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
   cudaIpcMemHandle_t h;
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, m.local);
   if (e != cudaSuccess) {

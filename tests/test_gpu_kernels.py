@@ -160,6 +160,38 @@ def test_reduce_two_streams(L):
     assert vals[0] == pytest.approx(oracle.sum_sq(xh), rel=RTOL_REDUCE)
 
 
+def test_reduce_first_use_of_fresh_nonblocking_streams(L):
+    """A stream's reduce scratch is zeroed in that stream's own order: first use
+    of fresh non-blocking streams while the legacy default stream is busy."""
+    rt = pytest.importorskip("cuda.bindings.runtime")
+    r = np.random.Generator(np.random.Philox(13))
+    xh = r.random(1 << 22, dtype=np.float32)
+    x = dev(xh)
+    want = oracle.sum_sq(xh)
+    big = torch.empty(1 << 28, device="cuda")
+    handles = []
+    try:
+        for _ in range(6):
+            err, h = rt.cudaStreamCreateWithFlags(rt.cudaStreamNonBlocking)
+            assert err == rt.cudaError_t.cudaSuccess
+            handles.append(h)
+        outs = [torch.full((1,), np.nan, dtype=torch.float64, device="cuda") for _ in handles]
+        torch.cuda.synchronize()
+        big.fill_(1.0)                        # queued on the legacy default stream
+        big.mul_(2.0)
+        for o, h in zip(outs, handles):
+            assert L.mk_mapreduce_f32(o.data_ptr(), x.data_ptr(), x.numel(), 1, 0, 0.0, int(h)) == 0
+        for h in handles:
+            rt.cudaStreamSynchronize(h)
+        torch.cuda.synchronize()
+        for o in outs:
+            assert o.item() == pytest.approx(want, rel=RTOL_REDUCE)
+    finally:
+        torch.cuda.synchronize()
+        for h in handles:
+            rt.cudaStreamDestroy(h)
+
+
 # -------------------------------------------------------------- gather -----
 
 def gather_dev(L, a_h, idx_h, off=0):
@@ -376,6 +408,53 @@ def test_findext_nan_and_signed_zero(L):
     assert findext_dev(L, z, True)[1] == 2
     assert findext_dev(L, np.float32([0.0, -0.0]), False)[1] == 2
     assert L.mk_findext_f32(0, 0, 0, 0, 1, stream()) == _lib.MK_ERR_INVALID
+
+
+def test_findext_large_ties_nan_zero(L):
+    # the vectorised main loop keeps one candidate per vector lane: ties,
+    # NaNs and signed zeros must still resolve to Julia's first-index answer
+    n = (1 << 22) + 5
+    x = np.full(n, 7.0, np.float32)
+    for fm in (True, False):
+        assert findext_dev(L, x, fm) == (7.0, 1)
+    x[3_000_001] = 9.0
+    x[2_000_003] = 9.0
+    assert findext_dev(L, x, True) == (9.0, 2_000_004)
+    x[1_500_002] = np.nan
+    x[1_000_001] = np.nan
+    for fm in (True, False):
+        v, i = findext_dev(L, x, fm)
+        assert np.isnan(v) and i == 1_000_002
+    z = np.full(n, -0.0, np.float32)
+    z[2_222_223] = 0.0
+    z[3_333_334] = 0.0
+    v, i = findext_dev(L, z, True)
+    assert i == 2_222_224 and v == 0.0 and not np.signbit(v)
+    assert findext_dev(L, z, False)[1] == 1
+    z[:] = 0.0
+    z[1_234_567] = -0.0
+    assert findext_dev(L, z, False)[1] == 1_234_568
+    assert findext_dev(L, z, True)[1] == 1
+
+
+def test_reduce_large_max_min_nan_and_signed_zero(L):
+    n = (1 << 22) + 7
+    z = np.full(n, -0.0, np.float32)
+    z[3_000_001] = 0.0
+    got = reduce_dev(L, dev(z), op="max", init=-np.inf)
+    assert got == 0.0 and not np.signbit(got)
+    z[:] = 0.0
+    z[2_000_003] = -0.0
+    got = reduce_dev(L, dev(z), op="min", init=np.inf)
+    assert got == 0.0 and np.signbit(got)
+    r = np.random.Generator(np.random.Philox(12))
+    x = r.standard_normal(n, dtype=np.float32)
+    assert reduce_dev(L, dev(x), op="max", init=-np.inf) == float(x.max())
+    assert reduce_dev(L, dev(x), op="min", init=np.inf) == float(x.min())
+    assert reduce_dev(L, dev(x), f="abs", op="max", init=-np.inf) == float(np.abs(x).max())
+    x[1_111_111] = np.nan
+    assert np.isnan(reduce_dev(L, dev(x), op="max", init=-np.inf))
+    assert np.isnan(reduce_dev(L, dev(x), op="min", init=np.inf))
 
 
 def test_findmax_surface(L):
