@@ -216,6 +216,94 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             return lambda: Lo.mlirb_sum_sq_f32(self.x_host.ctypes.data, self.n, 256, tmp.ctypes.data), \
                 self.units_per_step, "full 2^28-element sum(x.^2): materialised x.^2 + fp32 block-tree rounds"
 
+    class Maximum(Workload):
+        name = "maximum"
+        metric = "maximum(x) HBM GB/s"
+        cfg = workloads.CONFIGS["reduce"]
+
+        def __init__(self):
+            super().__init__(rank, world)
+            n = self.n = n_override or self.cfg["n"]
+            self.x_host = workloads.uniform_pm1(n, stream=3 + 100 * rank)
+            self.x = mk.MLIRArray(self.x_host)
+            self.out = torch.empty(1, dtype=torch.float64, device="cuda")
+            self.units_per_step = 4.0 * n
+            self.h2d_bytes, self.d2h_bytes = 4 * n, 8
+            self.config = {"workload": "maximum(x) via mapreducedim!, Float32 x ~ U[-1,1), n=2^28 per GPU "
+                                       "(scope row f1); Julia max semantics, exact", "n_per_gpu": n,
+                           "l2": "input (1 GiB) larger than L2; no flush"}
+
+        def launch(self):
+            _lib.check(L.mk_mapreduce_f32(self.out.data_ptr(), self.x.pointer(), self.n, 0, 1, float("-inf"),
+                                          stream()), "maximum")
+
+        def combine(self):
+            pass
+
+        def check(self):
+            assert self.out.item() == float(self.x_host.max())
+
+        def e2e_setup(self):
+            self.pinned = torch.from_numpy(self.x_host).pin_memory()
+            self.xd = mk.allocate(be, "Float32", self.n)
+
+        def e2e_step(self):
+            mk.copyto(be, self.xd, self.pinned)
+            return mk.maximum(self.xd)
+
+        def cpu_sample(self, threads):
+            import ctypes as C
+            import oracle
+            Lo = oracle.lib()
+            v = C.c_double()
+            return lambda: Lo.mlirb_findext_f32(C.byref(v), self.x_host.ctypes.data, self.n, 1), \
+                self.units_per_step, "full 2^28-element maximum (Julia order), OpenMP chunks + ordered combine"
+
+    class FindMax(Workload):
+        name = "findmax"
+        metric = "findmax(x) HBM GB/s"
+        cfg = workloads.CONFIGS["reduce"]
+
+        def __init__(self):
+            super().__init__(rank, world)
+            n = self.n = n_override or self.cfg["n"]
+            self.x_host = workloads.uniform_pm1(n, stream=4 + 100 * rank)
+            self.x = mk.MLIRArray(self.x_host)
+            self.val = torch.empty(1, dtype=torch.float64, device="cuda")
+            self.idx = torch.empty(1, dtype=torch.int64, device="cuda")
+            self.units_per_step = 4.0 * n
+            self.h2d_bytes, self.d2h_bytes = 4 * n, 16
+            self.config = {"workload": "findmax(x) (value, first 1-based index), Float32 x ~ U[-1,1), n=2^28 per "
+                                       "GPU (scope row f1); Julia order: NaN wins, +0 above -0, first index",
+                           "n_per_gpu": n, "l2": "input (1 GiB) larger than L2; no flush"}
+
+        def launch(self):
+            _lib.check(L.mk_findext_f32(self.val.data_ptr(), self.idx.data_ptr(), self.x.pointer(), self.n, 1,
+                                        stream()), "findmax")
+
+        def combine(self):
+            pass
+
+        def check(self):
+            import oracle
+            assert (self.val.item(), self.idx.item()) == oracle.findext(self.x_host, True)
+
+        def e2e_setup(self):
+            self.pinned = torch.from_numpy(self.x_host).pin_memory()
+            self.xd = mk.allocate(be, "Float32", self.n)
+
+        def e2e_step(self):
+            mk.copyto(be, self.xd, self.pinned)
+            return mk.findmax(self.xd)
+
+        def cpu_sample(self, threads):
+            import ctypes as C
+            import oracle
+            Lo = oracle.lib()
+            v = C.c_double()
+            return lambda: Lo.mlirb_findext_f32(C.byref(v), self.x_host.ctypes.data, self.n, 1), \
+                self.units_per_step, "full 2^28-element findmax, OpenMP chunks + ordered combine"
+
     class Vadd(Workload):
         name = "vadd"
         metric = "vadd HBM GB/s"
@@ -570,7 +658,8 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
                                                    self.m, self.nn, self.k, self.m, self.k, self.m, 0, cols), \
                 2.0 * self.m * cols * self.k, f"C[:, 1:{cols}] of the 8192^3 product (restated 16x16 tiles)"
 
-    table = {"reduce": Reduce, "vadd": Vadd, "gather": Gather, "histogram": Histogram,
+    table = {"reduce": Reduce, "maximum": Maximum, "findmax": FindMax, "vadd": Vadd, "gather": Gather,
+             "histogram": Histogram,
              "matmul": Matmul, "matmul_simt": MatmulSimt,
              "scan": Scan, "reduce_dims": Dims}
     return table[kind]()
@@ -826,15 +915,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--kernel", default="reduce",
-                    choices=["reduce", "vadd", "gather", "histogram", "matmul", "matmul_simt", "scan", "reduce_dims",
-                             "all"])
+                    choices=["reduce", "maximum", "findmax", "vadd", "gather", "histogram", "matmul", "matmul_simt",
+                             "scan", "reduce_dims", "all"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--n", type=int, default=None,
                     help="override the element count of the configuration (small profiling cases)")
     args = ap.parse_args()
-    kinds = (["reduce", "vadd", "gather", "histogram", "matmul", "matmul_simt", "scan", "reduce_dims"]
+    kinds = (["reduce", "maximum", "findmax", "vadd", "gather", "histogram", "matmul", "matmul_simt", "scan",
+              "reduce_dims"]
              if args.kernel == "all" else [args.kernel])
 
     rank = int(os.environ.get("RANK", "0"))
@@ -857,7 +947,7 @@ def main():
     if world > 1:
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
-    defaults = {"reduce": (2000, 50), "vadd": (2000, 50), "gather": (200, 10), "histogram": (500, 20),
+    defaults = {"reduce": (2000, 50), "maximum": (1000, 20), "findmax": (1000, 20), "vadd": (2000, 50), "gather": (200, 10), "histogram": (500, 20),
                 "matmul": (20, 3), "matmul_simt": (3, 1), "scan": (500, 20), "reduce_dims": (1000, 20)}
     try:
         for k in kinds:

@@ -13,6 +13,7 @@
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int kVec = 8;  // float4 loads in flight per thread
 
 struct Cand {
   float v;
@@ -33,6 +34,26 @@ __device__ __forceinline__ bool better(float a, int64_t ia, float b, int64_t ib)
     return ia < ib;
   }
   return MAX ? a > b : a < b;
+}
+
+// Julia's order as an unsigned key, larger = preferred: the float bits made
+// monotone (negative values complemented, so -0 ranks below +0), complemented
+// again for findmin, and every NaN mapped to the largest key (NaN wins both).
+// No value maps to 0.
+template <bool MAX>
+__device__ __forceinline__ uint32_t order_key(float v) {
+  const uint32_t u = __float_as_uint(v);
+  uint32_t k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  if (!MAX) k = ~k;
+  return v != v ? 0xFFFFFFFFu : k;
+}
+
+// The value a key came from (every NaN comes back as the canonical NaN).
+template <bool MAX>
+__device__ __forceinline__ float key_value(uint32_t k) {
+  if (k == 0xFFFFFFFFu) return __uint_as_float(0x7FC00000u);
+  if (!MAX) k = ~k;
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
 template <bool MAX>
@@ -66,7 +87,7 @@ __device__ Cand block_best(Cand c, Cand* sm) {
 }
 
 template <bool MAX>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 6)
 findext_kernel(const float* __restrict__ x, int64_t n, int head, float* __restrict__ pv, int64_t* __restrict__ pi,
                unsigned* __restrict__ ticket, double* __restrict__ val_out, int64_t* __restrict__ idx_out) {
   __shared__ Cand sm[kThreads / 32];
@@ -77,13 +98,46 @@ findext_kernel(const float* __restrict__ x, int64_t n, int head, float* __restri
   Cand c{MAX ? -INFINITY : INFINITY, INT64_MAX};
   const float4* x4 = reinterpret_cast<const float4*>(x + head);
   const int64_t n4 = (n - head) / 4;
-  for (int64_t i = tid; i < n4; i += stride) {
-    const float4 q = __ldcs(x4 + i);
-    const int64_t e = head + 4 * i;
-    keep<MAX>(c, q.x, e);
-    keep<MAX>(c, q.y, e + 1);
-    keep<MAX>(c, q.z, e + 2);
-    keep<MAX>(c, q.w, e + 3);
+  {
+    // One candidate per vector lane, kVec vectors in flight.  Each value is
+    // ranked by an unsigned key in Julia's order (see order_key), so a step is
+    // one compare; a chain visits increasing indices, so the strict compare
+    // keeps the first index among equals.  Chains and threads then combine
+    // with the same rule (greater key, else lower index).
+    uint32_t bk[4] = {0u, 0u, 0u, 0u};  // 0: no candidate (no value maps to 0)
+    int64_t bi[4] = {INT64_MAX, INT64_MAX, INT64_MAX, INT64_MAX};
+    auto step = [&](int l, float v, int64_t e) {
+      const uint32_t k = order_key<MAX>(v);
+      if (k > bk[l]) {
+        bk[l] = k;
+        bi[l] = e;
+      }
+    };
+    int64_t i = tid;
+    for (; i + (kVec - 1) * stride < n4; i += kVec * stride) {
+      float4 q[kVec];
+#pragma unroll
+      for (int u = 0; u < kVec; ++u) q[u] = __ldcs(x4 + i + u * stride);
+#pragma unroll
+      for (int u = 0; u < kVec; ++u) {
+        const int64_t e = head + 4 * (i + u * stride);
+        step(0, q[u].x, e);
+        step(1, q[u].y, e + 1);
+        step(2, q[u].z, e + 2);
+        step(3, q[u].w, e + 3);
+      }
+    }
+    for (; i < n4; i += stride) {
+      const float4 q = __ldcs(x4 + i);
+      const int64_t e = head + 4 * i;
+      step(0, q.x, e);
+      step(1, q.y, e + 1);
+      step(2, q.z, e + 2);
+      step(3, q.w, e + 3);
+    }
+#pragma unroll
+    for (int l = 0; l < 4; ++l)
+      if (bk[l] != 0u) keep<MAX>(c, key_value<MAX>(bk[l]), bi[l]);
   }
   const int64_t tail = head + 4 * n4;
   if (tid < head) keep<MAX>(c, x[tid], tid);
@@ -108,6 +162,13 @@ findext_kernel(const float* __restrict__ x, int64_t n, int head, float* __restri
   }
 }
 
+template <typename Kernel>
+int resident_per_sm(Kernel k) {
+  int b = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k, kThreads, 0) != cudaSuccess || b < 1) b = 1;
+  return b;
+}
+
 }  // namespace
 
 extern "C" int mk_findext_f32(double* val_out, int64_t* idx_out, const float* x, int64_t n, int find_max,
@@ -130,8 +191,11 @@ extern "C" int mk_findext_f32(double* val_out, int64_t* idx_out, const float* x,
   if (e != cudaSuccess) return mk::fail_cuda(e, "mk_findext_f32: ticket");
   int64_t head = (int64_t)(((16u - (reinterpret_cast<uintptr_t>(x) & 15u)) & 15u) / 4u);
   if (head > n) head = n;
+  // persistent grid: as many blocks as are resident at once (one wave)
+  static const int per_sm[2] = {resident_per_sm(findext_kernel<false>), resident_per_sm(findext_kernel<true>)};
   int64_t blocks = mk::cdiv(n, (int64_t)kThreads * 16);
-  const int64_t cap = (int64_t)dev->sms * 8 < kMaxBlocks ? (int64_t)dev->sms * 8 : kMaxBlocks;
+  int64_t cap = (int64_t)dev->sms * per_sm[find_max ? 1 : 0];
+  if (cap > kMaxBlocks) cap = kMaxBlocks;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   if (find_max)

@@ -185,9 +185,21 @@ mapreduce_kernel(const float* __restrict__ x, int64_t n, int head, double init,
   }
 }
 
+// The grid is persistent: never more blocks than fit on the GPU at once (the
+// resident count depends on each instantiation's registers), so no block
+// waits for a second wave.
 template <int F, int OP>
 void launch(unsigned blocks, cudaStream_t s, const float* x, int64_t n, int head, double init,
             const mk::ReduceScratch& rs, double* out, const mk::PeerArgs& peer, unsigned* err) {
+  static const int per_sm = [] {
+    int b = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, mapreduce_kernel<F, OP>, kThreads, 0) != cudaSuccess)
+      b = 1;
+    return b > 0 ? b : 1;
+  }();
+  const mk::Device* dev = mk::current_device();
+  const unsigned resident = (unsigned)((dev ? dev->sms : 1) * per_sm);
+  if (blocks > resident) blocks = resident;
   mapreduce_kernel<F, OP><<<blocks, kThreads, 0, s>>>(x, n, head, init, rs.partials, rs.ticket, out, peer, err);
 }
 

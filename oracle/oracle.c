@@ -163,6 +163,40 @@ int64_t or_findext_f32(double* val, const float* x, int64_t n, int find_max) {
   return best + 1;
 }
 
+/* CPU-baseline findmax/findmin: each OpenMP thread runs the or_findext_f32
+ * rule over a contiguous chunk, and the chunk winners are combined in chunk
+ * order with the same rule (an earlier chunk wins ties, so the first index
+ * wins overall).  Returns the 1-based index. */
+static int fe_better(float a, int64_t ia, float b, int64_t ib, int find_max) {
+  if (a != a || b != b) return (a != a) && (!(b != b) || ia < ib);
+  if (a == b) {
+    if (signbit(a) != signbit(b)) return find_max ? !signbit(a) : signbit(a);
+    return ia < ib;
+  }
+  return find_max ? a > b : a < b;
+}
+
+int64_t mlirb_findext_f32(double* val, const float* x, int64_t n, int find_max) {
+  if (n <= 0) return 0;
+  const int T = omp_get_max_threads();
+  int64_t* best = (int64_t*)malloc(sizeof(int64_t) * (size_t)T);
+#pragma omp parallel num_threads(T)
+  {
+    const int t = omp_get_thread_num(), nt = omp_get_num_threads();
+    const int64_t lo = n * t / nt, hi = n * (t + 1) / nt;
+    int64_t b = lo;
+    for (int64_t i = lo + 1; i < hi; ++i)
+      if (fe_better(x[i], i, x[b], b, find_max)) b = i;
+    best[t] = hi > lo ? b : -1;
+  }
+  int64_t b = -1;
+  for (int t = 0; t < T; ++t)
+    if (best[t] >= 0 && (b < 0 || fe_better(x[best[t]], best[t], x[b], b, find_max))) b = best[t];
+  free(best);
+  *val = (double)x[b];
+  return b + 1;
+}
+
 /* gather: c[i] = a[idx[i]], 1-based (src/lower.jl:4064-4077).  An index out of
  * [1, na] writes 0 and reports OR_ERR_DEVICE_FAULT (the reference raises a
  * BoundsError/KernelException without @inbounds). */

@@ -55,3 +55,25 @@ def test_mm_tiled16_bitexact_with_checker():
     Cm = np.zeros((M, N), dtype=np.float32, order="F")
     assert L.mlirb_mm_tiled16_f32(p(Cm), p(A), p(B), M, N, K, M, K, M, 0, N) == 0
     np.testing.assert_array_equal(Cm, oracle.mm_tiled16_f32(A, B))
+
+
+@pytest.mark.parametrize("find_max", [1, 0])
+def test_mlirb_findext_matches_checker(find_max):
+    """The OpenMP findmax/findmin baseline agrees with the sequential checker:
+    first index among ties, NaN wins both, +0.0 above -0.0 (chunk borders included)."""
+    import ctypes as C
+    r = np.random.Generator(np.random.Philox(21))
+    for n in (1, 2, 7, 1000, 100_003):
+        x = r.standard_normal(n, dtype=np.float32)
+        x[n // 3] = x[n // 2] = x.max() if find_max else x.min()
+        for case in range(3):
+            y = x.copy()
+            if case == 1 and n > 10:
+                y[n // 5] = y[(4 * n) // 5] = np.nan
+            if case == 2:
+                y[:] = -0.0
+                y[n // 2:] = 0.0
+            v = C.c_double()
+            got = oracle.lib().mlirb_findext_f32(C.byref(v), y.ctypes.data, n, find_max)
+            assert got == oracle.findext(y, bool(find_max))[1]
+
