@@ -808,9 +808,11 @@ PROFILED_TRAFFIC: dict[str, float | None] = {
     "vadd": 8398336 + 0,                  # vadd_f32_vec4, n = 2^20 (stores stay in L2)
     "gather": 14957786368 + 536444160,    # gather_f32_vec4 (.cg loads), n = 2^27
     "histogram": 268520960 + 5512192,     # hist_smem, n = 2^26
-    "matmul": 4584232704 + 257805056,     # sgemm_tf32x3, 8192^3 (split pre-pass excluded)
+    "matmul": 5886670080 + 275036672,     # sgemm_tf32x3_pair, 8192^3 (split pre-pass excluded)
     "scan": 1074146816 + 1024940032,      # scan_kernel (look-back), n = 2^28
-    "reduce_dims": 1073759232 + 2959872,  # seg_warp, 16384 x 16384, dims=1
+    "reduce_dims": 1073759744 + 3271168,  # seg_warp (16-byte loads), 16384 x 16384, dims=1
+    "maximum": 1073788672 + 3324672,      # mapreduce_kernel<identity,max>, n = 2^28
+    "findmax": 1073792000 + 3548928,      # findext_kernel<true>, n = 2^28
 }
 
 
