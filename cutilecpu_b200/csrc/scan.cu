@@ -58,17 +58,70 @@ __device__ __forceinline__ unsigned long long peek(const unsigned long long* p) 
   return w;
 }
 
-__device__ __forceinline__ int pad(int i) { return i + (i >> 5); }
+// Decoupled look-back for tile t, run by one whole warp: publishes the tile's
+// aggregate, combines the predecessors' words 32 at a time back to the
+// nearest inclusive prefix, publishes the tile's inclusive prefix and returns
+// the exclusive prefix.  The wait is bounded: on timeout ERRBIT_TIMEOUT is
+// raised and `init` is used, so no successor waits forever.
+template <int OP>
+__device__ double look_back(ScanState st, int64_t t, double block_total, double init, unsigned long long limit,
+                            unsigned* err) {
+  const int lane = threadIdx.x & 31;
+  double prefix;
+  if (t == 0) {
+    prefix = init;
+  } else {
+    if (lane == 0) publish(st.word + t, pack(block_total, 0u));
+    double acc = neutral<OP>();
+    int64_t j = t - 1 - lane;  // lane i looks at tile t-1-i
+    bool found = false, timed_out = false;
+    const long long t0 = clock64();
+    while (!found) {
+      unsigned long long w = (j >= 0) ? peek(st.word + j) : pack(init, 1u);
+      // wait (warp-uniformly) until every lane of the window sees a value
+      while (!__all_sync(0xffffffffu, w != EMPTY)) {
+        if (__any_sync(0xffffffffu, (unsigned long long)(clock64() - t0) > limit)) {
+          timed_out = true;
+          break;
+        }
+        if (w == EMPTY) w = peek(st.word + j);
+      }
+      if (timed_out) break;
+      const unsigned incl = __ballot_sync(0xffffffffu, (w & 1ull) != 0ull);
+      const int stop = incl ? __ffs(incl) - 1 : 32;  // nearest lane holding an inclusive prefix
+      double part = (lane <= stop) ? unpack(w) : neutral<OP>();
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) part = combine<OP>(part, __shfl_xor_sync(0xffffffffu, part, o));
+      acc = combine<OP>(part, acc);
+      if (stop < 32) found = true;
+      j -= 32;
+    }
+    if (timed_out) {
+      if (lane == 0) atomicOr(err, mk::ERRBIT_TIMEOUT);
+      acc = init;
+    }
+    prefix = acc;
+  }
+  if (lane == 0) publish(st.word + t, pack(combine<OP>(prefix, block_total), 1u));
+  return prefix;
+}
 
-template <int OP, int kPer>
+constexpr int kPer = 32;                 // elements per thread: one 128-byte row
+constexpr int kTile = kThreads * kPer;   // 8192 elements per tile
+
+// Shared-memory tile: row r (thread r's 32 values) is 8 16-byte chunks, and
+// chunk c of row r is stored at slot c ^ (r & 7).  A thread then reads and
+// writes its row as 8 conflict-free 16-byte accesses (a quarter-warp touches
+// 8 rows at 8 distinct bank groups), and the coalesced global loads/stores
+// (8 consecutive float4 = one row) are conflict-free too.
+__device__ __forceinline__ int slot(int r, int c) { return r * 8 + (c ^ (r & 7)); }
+
+template <int OP>
 __global__ void __launch_bounds__(kThreads)
 scan_kernel(float* out, const float* x,  // may alias: a tile reads all of its input before writing
             int64_t n, double init, int exclusive,
             ScanState st, unsigned long long limit, unsigned* __restrict__ err) {
-  constexpr int kTile = kThreads * kPer;
-  // one pad word per 32 floats: a thread's consecutive values and a warp's
-  // float4 columns both map to 32 distinct banks
-  extern __shared__ float buf[];  // kTile + kTile / 32 floats
+  extern __shared__ float4 buf4[];  // kTile / 4 chunks
   __shared__ double warp_tot[kThreads / 32];
   __shared__ unsigned s_tile;
   __shared__ double s_prefix;
@@ -78,35 +131,42 @@ scan_kernel(float* out, const float* x,  // may alias: a tile reads all of its i
   const int64_t t = s_tile;
   const int64_t base = t * kTile;
   const int64_t cnt = min((int64_t)kTile, n - base);
+  const bool vec = cnt == kTile && ((reinterpret_cast<uintptr_t>(x + base) & 15u) == 0);
 
-  // coalesced load into shared memory
-  if (cnt == kTile && ((reinterpret_cast<uintptr_t>(x + base) & 15u) == 0)) {
+  // coalesced load into shared memory; past the end of x: the neutral element
+  if (vec) {
     const float4* src = reinterpret_cast<const float4*>(x + base);
+    float4 q[kPer / 4];
+#pragma unroll
+    for (int i = 0; i < kPer / 4; ++i) q[i] = __ldcs(src + i * kThreads + tid);
 #pragma unroll
     for (int i = 0; i < kPer / 4; ++i) {
-      const int e = 4 * (i * kThreads + tid);
-      const float4 q = __ldcs(src + i * kThreads + tid);
-      buf[pad(e)] = q.x;
-      buf[pad(e + 1)] = q.y;
-      buf[pad(e + 2)] = q.z;
-      buf[pad(e + 3)] = q.w;
+      const int f = i * kThreads + tid;
+      buf4[slot(f >> 3, f & 7)] = q[i];
     }
   } else {
-    for (int i = tid; i < kTile; i += kThreads) buf[pad(i)] = i < cnt ? x[base + i] : 0.0f;
+    float* buf = reinterpret_cast<float*>(buf4);
+    for (int e = tid; e < kTile; e += kThreads)
+      buf[slot(e >> 5, (e >> 2) & 7) * 4 + (e & 3)] = e < cnt ? x[base + e] : neutral32<OP>();
   }
   __syncthreads();
 
-  // per-thread total of its kPer values: an fp32 pairwise tree (relative
-  // error <= log2(kPer) ulp of the sum of magnitudes), widened to fp64 for
-  // the carries.  The values are re-read from shared memory for the output
-  // pass, which keeps registers (and so occupancy) free for more tiles.
+  float4* row = buf4 + tid * 8;
+  const int sw = tid & 7;
+  // per-thread total of its 32 values: an fp32 pairwise tree (relative error
+  // <= 5 ulp of the sum of magnitudes), widened to fp64 for the carries.  The
+  // values are re-read from shared memory for the output pass, which keeps
+  // registers (and so occupancy) free for more tiles.
   double run;
   {
     float v[kPer];
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int idx = tid * kPer + j;
-      v[j] = idx < cnt ? buf[pad(idx)] : neutral32<OP>();
+    for (int c = 0; c < 8; ++c) {
+      const float4 q = row[c ^ sw];
+      v[4 * c] = q.x;
+      v[4 * c + 1] = q.y;
+      v[4 * c + 2] = q.z;
+      v[4 * c + 3] = q.w;
     }
 #pragma unroll
     for (int w = 1; w < kPer; w <<= 1)
@@ -134,96 +194,50 @@ scan_kernel(float* out, const float* x,  // may alias: a tile reads all of its i
 
   // decoupled look-back (warp 0)
   if (warp == 0) {
-    double prefix;
-    if (t == 0) {
-      prefix = init;
-    } else {
-      if (lane == 0) publish(st.word + t, pack(block_total, 0u));
-      double acc = neutral<OP>();
-      int64_t j = t - 1 - lane;  // lane i looks at tile t-1-i
-      bool found = false, timed_out = false;
-      const long long t0 = clock64();
-      while (!found) {
-        unsigned long long w = (j >= 0) ? peek(st.word + j) : pack(init, 1u);
-        // wait (warp-uniformly) until every lane of the window sees a value
-        while (!__all_sync(0xffffffffu, w != EMPTY)) {
-          if (__any_sync(0xffffffffu, (unsigned long long)(clock64() - t0) > limit)) {
-            timed_out = true;
-            break;
-          }
-          if (w == EMPTY) w = peek(st.word + j);
-        }
-        if (timed_out) break;
-        const unsigned incl = __ballot_sync(0xffffffffu, (w & 1ull) != 0ull);
-        const int stop = incl ? __ffs(incl) - 1 : 32;  // nearest lane holding an inclusive prefix
-        double part = (lane <= stop) ? unpack(w) : neutral<OP>();
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) part = combine<OP>(part, __shfl_xor_sync(0xffffffffu, part, o));
-        acc = combine<OP>(part, acc);
-        if (stop < 32) found = true;
-        j -= 32;
-      }
-      if (timed_out) {
-        if (lane == 0) atomicOr(err, mk::ERRBIT_TIMEOUT);
-        acc = init;
-      }
-      prefix = acc;
-    }
-    if (lane == 0) {
-      publish(st.word + t, pack(combine<OP>(prefix, block_total), 1u));
-      s_prefix = prefix;
-    }
+    const double prefix = look_back<OP>(st, (int64_t)t, block_total, init, limit, err);
+    if (lane == 0) s_prefix = prefix;
   }
   __syncthreads();
   // output: the fp64 thread prefix rounded once to fp32, then an fp32
-  // running combination of the thread's own values (<= kPer terms)
+  // running combination of the thread's own values (<= 32 terms); values past
+  // the end are the neutral element and are never stored
   const float pre = (float)combine<OP>(s_prefix, texcl);
   float loc = neutral32<OP>();
-#pragma unroll 8
-  for (int j = 0; j < kPer; ++j) {
-    const int idx = tid * kPer + j;
-    const float before = combine32<OP>(pre, loc);
-    if (idx < cnt) loc = combine32<OP>(loc, buf[pad(idx)]);
-    buf[pad(idx)] = exclusive ? before : combine32<OP>(pre, loc);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const float4 q = row[c ^ sw];
+    const float in[4] = {q.x, q.y, q.z, q.w};
+    float o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float before = combine32<OP>(pre, loc);
+      loc = combine32<OP>(loc, in[e]);
+      o[e] = exclusive ? before : combine32<OP>(pre, loc);
+    }
+    row[c ^ sw] = make_float4(o[0], o[1], o[2], o[3]);
   }
   __syncthreads();
   if (cnt == kTile && ((reinterpret_cast<uintptr_t>(out + base) & 15u) == 0)) {
     float4* dst = reinterpret_cast<float4*>(out + base);
 #pragma unroll
     for (int i = 0; i < kPer / 4; ++i) {
-      const int e = 4 * (i * kThreads + tid);
-      __stcs(dst + i * kThreads + tid, make_float4(buf[pad(e)], buf[pad(e + 1)], buf[pad(e + 2)], buf[pad(e + 3)]));
+      const int f = i * kThreads + tid;
+      __stcs(dst + f, buf4[slot(f >> 3, f & 7)]);
     }
   } else {
-    for (int i = tid; i < cnt; i += kThreads) out[base + i] = buf[pad(i)];
+    const float* buf = reinterpret_cast<const float*>(buf4);
+    for (int e = tid; e < cnt; e += kThreads) out[base + e] = buf[slot(e >> 5, (e >> 2) & 7) * 4 + (e & 3)];
   }
 }
 
-// elements per thread (tuning knob MK_TUNE_SCAN_PER: 16, 32 or 64)
-int scan_per() {
-  static int v = [] {
-    const char* e = getenv("MK_TUNE_SCAN_PER");
-    int p = e ? atoi(e) : 32;
-    return (p == 16 || p == 32 || p == 64) ? p : 32;
-  }();
-  return v;
-}
-
-template <int OP, int PER>
-int launch_per(int64_t tiles, size_t smem, cudaStream_t s, float* out, const float* x, int64_t n, double init,
-               int exclusive, ScanState st, unsigned long long limit, unsigned* err) {
-  int rc = mk::allow_dynamic_smem(reinterpret_cast<const void*>(scan_kernel<OP, PER>), smem);
-  if (rc != MK_OK) return rc;
-  scan_kernel<OP, PER><<<(unsigned)tiles, kThreads, smem, s>>>(out, x, n, init, exclusive, st, limit, err);
-  return MK_OK;
-}
-
 template <int OP>
-int launch(int per, int64_t tiles, size_t smem, cudaStream_t s, float* out, const float* x, int64_t n, double init,
-           int exclusive, ScanState st, unsigned long long limit, unsigned* err) {
-  if (per == 16) return launch_per<OP, 16>(tiles, smem, s, out, x, n, init, exclusive, st, limit, err);
-  if (per == 64) return launch_per<OP, 64>(tiles, smem, s, out, x, n, init, exclusive, st, limit, err);
-  return launch_per<OP, 32>(tiles, smem, s, out, x, n, init, exclusive, st, limit, err);
+int launch(int64_t tiles, cudaStream_t s, float* out, const float* x, int64_t n, double init, int exclusive,
+           ScanState st, unsigned long long limit, unsigned* err) {
+  constexpr size_t smem = (size_t)kTile * sizeof(float);
+  int rc = mk::allow_dynamic_smem(reinterpret_cast<const void*>(scan_kernel<OP>), smem);
+  if (rc != MK_OK) return rc;
+  scan_kernel<OP><<<(unsigned)tiles, kThreads, smem, s>>>(out, x, n, init, exclusive, st, limit, err);
+  return MK_OK;
 }
 
 }  // namespace
@@ -235,7 +249,7 @@ extern "C" int mk_accumulate_f32(float* out, const float* x, int64_t n, int op, 
   if (op < MK_OP_ADD || op > MK_OP_MUL) return mk::fail(MK_ERR_INVALID, "mk_accumulate_f32: unknown op");
   if (n == 0) return MK_OK;
   if (!out || !x) return mk::fail(MK_ERR_INVALID, "mk_accumulate_f32: null pointer");
-  const int64_t tiles = mk::cdiv(n, (int64_t)kThreads * scan_per());
+  const int64_t tiles = mk::cdiv(n, (int64_t)kTile);
   if (tiles > (int64_t)UINT32_MAX / 2) return mk::fail(MK_ERR_INVALID, "mk_accumulate_f32: n too large");
   cudaStream_t s = mk::as_stream(stream);
   // workspace: [counter (256 B) | one state word per tile]
@@ -248,13 +262,11 @@ extern "C" int mk_accumulate_f32(float* out, const float* x, int64_t n, int op, 
   if (e == cudaSuccess) e = cudaMemsetAsync(b + 256, 0xFF, (size_t)tiles * 8, s);  // every tile EMPTY
   if (e != cudaSuccess) return mk::fail_cuda(e, "mk_accumulate_f32: clearing tile state");
   const unsigned long long limit = mk::wait_limit_cycles();
-  const int per = scan_per();
-  const size_t smem = (size_t)(kThreads * per + kThreads * per / 32) * sizeof(float);
   switch (op) {
-    case MK_OP_ADD: rc = launch<MK_OP_ADD>(per, tiles, smem, s, out, x, n, init, exclusive, st, limit, dev->err_word); break;
-    case MK_OP_MAX: rc = launch<MK_OP_MAX>(per, tiles, smem, s, out, x, n, init, exclusive, st, limit, dev->err_word); break;
-    case MK_OP_MIN: rc = launch<MK_OP_MIN>(per, tiles, smem, s, out, x, n, init, exclusive, st, limit, dev->err_word); break;
-    default: rc = launch<MK_OP_MUL>(per, tiles, smem, s, out, x, n, init, exclusive, st, limit, dev->err_word); break;
+    case MK_OP_ADD: rc = launch<MK_OP_ADD>(tiles, s, out, x, n, init, exclusive, st, limit, dev->err_word); break;
+    case MK_OP_MAX: rc = launch<MK_OP_MAX>(tiles, s, out, x, n, init, exclusive, st, limit, dev->err_word); break;
+    case MK_OP_MIN: rc = launch<MK_OP_MIN>(tiles, s, out, x, n, init, exclusive, st, limit, dev->err_word); break;
+    default: rc = launch<MK_OP_MUL>(tiles, s, out, x, n, init, exclusive, st, limit, dev->err_word); break;
   }
   if (rc != MK_OK) return rc;
   return mk::check_launch("mk_accumulate_f32: launch");
