@@ -169,28 +169,50 @@ __global__ void __launch_bounds__(256) split_a(float* __restrict__ A2, const flo
 }
 
 // B (K x N column-major, ldb) -> B2 (N rows x 2Kt): already K-major, so B2 is
-// written linearly, 8 lanes per (column n, k-block) segment.  VEC: B and ldb
-// allow 16-byte loads.
+// written linearly.  A thread takes one source float4 (4 consecutive k of one
+// column n) per step and writes its hi part into float4 q and its lo part into
+// float4 4 + q of the (n, k-block) segment; two steps are in flight per
+// thread.  VEC: B and ldb allow 16-byte loads.
+template <bool VEC>
+__device__ __forceinline__ float4 load_b4(const float* __restrict__ B, int64_t ldb, int nkb, int64_t kvalid,
+                                          int64_t src, int64_t& seg, int& q) {
+  seg = src >> 2;
+  q = (int)(src & 3);
+  const int64_t n = seg / nkb;
+  const int kb = (int)(seg - n * nkb);
+  const int64_t k = (int64_t)kb * KB + 4 * q;
+  const float* p = B + n * ldb + k;
+  if (VEC && k + 4 <= kvalid) return *reinterpret_cast<const float4*>(p);
+  // unaligned B, or the zero-padded K remainder
+  return make_float4(k < kvalid ? p[0] : 0.0f, k + 1 < kvalid ? p[1] : 0.0f, k + 2 < kvalid ? p[2] : 0.0f,
+                     k + 3 < kvalid ? p[3] : 0.0f);
+}
+
 template <bool VEC>
 __global__ void __launch_bounds__(256) split_b(float* __restrict__ B2, const float* __restrict__ B, int64_t N,
                                                int64_t ldb, int nkb, int64_t kvalid) {
-  const int64_t total = N * (int64_t)nkb * 8;  // float4 outputs
+  const int64_t total = N * (int64_t)nkb * 4;  // source float4s
   const int64_t stride = (int64_t)gridDim.x * 256;
-  for (int64_t t = (int64_t)blockIdx.x * 256 + threadIdx.x; t < total; t += stride) {
-    const int64_t seg = t >> 3;
-    const int i = (int)(t & 7);
-    const int64_t n = seg / nkb;
-    const int kb = (int)(seg - n * nkb);
-    const int64_t k = (int64_t)kb * KB + 4 * (i & 3);
-    const float* src = B + n * ldb + k;
-    float4 x;
-    if (VEC && k + 4 <= kvalid) {
-      x = *reinterpret_cast<const float4*>(src);
-    } else {  // unaligned B, or the zero-padded K remainder
-      x = make_float4(k < kvalid ? src[0] : 0.0f, k + 1 < kvalid ? src[1] : 0.0f, k + 2 < kvalid ? src[2] : 0.0f,
-                      k + 3 < kvalid ? src[3] : 0.0f);
-    }
-    reinterpret_cast<float4*>(B2)[t] = segment_part(x, i);
+  float4* out = reinterpret_cast<float4*>(B2);
+  int64_t t = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  for (; t + stride < total; t += 2 * stride) {
+    int64_t s0, s1;
+    int q0, q1;
+    const float4 x0 = load_b4<VEC>(B, ldb, nkb, kvalid, t, s0, q0);
+    const float4 x1 = load_b4<VEC>(B, ldb, nkb, kvalid, t + stride, s1, q1);
+    const float4 h0 = hi4(x0), h1 = hi4(x1);
+    out[s0 * 8 + q0] = h0;
+    out[s0 * 8 + 4 + q0] = lo4(x0, h0);
+    out[s1 * 8 + q1] = h1;
+    out[s1 * 8 + 4 + q1] = lo4(x1, h1);
+  }
+  for (; t < total; t += stride) {
+    int64_t s0;
+    int q0;
+    const float4 x0 = load_b4<VEC>(B, ldb, nkb, kvalid, t, s0, q0);
+    const float4 h0 = hi4(x0);
+    out[s0 * 8 + q0] = h0;
+    out[s0 * 8 + 4 + q0] = lo4(x0, h0);
   }
 }
 
@@ -711,7 +733,7 @@ int sgemm_impl(const char* name, bool full_k, float* C, const float* A, const fl
 
   split_a<<<dim3((unsigned)mk::cdiv(M, SA_ROWS), (unsigned)mk::cdiv(nkb, SA_KBS)), 256, 0, s>>>(A2, A, M, lda, nkb, kvalid);
   {
-    const int64_t total = N * (int64_t)nkb * 8;
+    const int64_t total = N * (int64_t)nkb * 4;
     int64_t blocks = mk::cdiv(total, 256);
     const int64_t cap = (int64_t)dev->sms * 8;
     if (blocks > cap) blocks = cap;
