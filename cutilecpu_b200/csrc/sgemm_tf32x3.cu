@@ -31,8 +31,8 @@
 //                  internal fp32 accumulation is biased (it does not round to
 //                  nearest); bounding it to 256 terms keeps the K=8192 result
 //                  within 1e-5 of fp64.  Finally coalesced column-major stores.
-// sgemm_tf32x3_pair (below, the default) runs the same pipeline on CTA pairs
-// with 256x256 tiles; MK_SGEMM_PAIR=0 selects the one-CTA kernel.
+// sgemm_tf32x3_pair (below) runs the same pipeline on CTA pairs with 256x256
+// tiles; it is used whenever those tiles fill every SM pair (see pair_mode).
 // Every mbarrier wait is bounded (mk::wait_limit_cycles); a timeout raises
 // ERRBIT_TIMEOUT in the device error word, stops the other roles, drains the
 // producer's in-flight copies (bounded), frees TMEM and returns.
@@ -691,13 +691,17 @@ int make_map(CUtensorMap* map, const float* base, uint64_t cols, uint64_t rows, 
 
 namespace {
 
-// MK_SGEMM_PAIR=0 selects the one-CTA kernel (128x256 tiles); default: CTA pairs.
-bool use_pair_kernel() {
-  static const bool on = [] {
+// Kernel choice: CTA pairs (256x256 tiles) when their tiles fill every SM
+// pair at least once, else one CTA per 128x256 tile (smaller tiles fill a
+// small problem better).  MK_SGEMM_PAIR=1 forces pairs, MK_SGEMM_PAIR=0 forbids them.
+int pair_mode() {
+  static const int mode = [] {
     const char* e = getenv("MK_SGEMM_PAIR");
-    return !(e && e[0] == '0');
+    if (e && e[0] == '0') return 0;
+    if (e && e[0] == '1') return 1;
+    return -1;
   }();
-  return on;
+  return mode;
 }
 
 // full_k: every K term (LinearAlgebra.mul!); otherwise 16*floor(K/16) terms
@@ -742,7 +746,8 @@ int sgemm_impl(const char* name, bool full_k, float* C, const float* A, const fl
     else
       split_b<false><<<(unsigned)blocks, 256, 0, s>>>(B2, B, N, ldb, nkb, kvalid);
   }
-  const bool pair = use_pair_kernel();
+  const int mode = pair_mode();
+  const bool pair = mode == 1 || (mode < 0 && mk::cdiv(N, 256) * mk::cdiv(M, 256) >= dev->sms / 2);
   CUtensorMap mapA, mapB;
   if ((rc = make_map(&mapA, A2, cols, (uint64_t)M, BM)) != MK_OK) return rc;
   if ((rc = make_map(&mapB, B2, cols, (uint64_t)N, pair ? P_BNH : BN)) != MK_OK) return rc;

@@ -142,3 +142,19 @@ def test_mul_and_mm_naive_surface(cuda):
     C2 = mk.zeros(mk.get_backend(Am), "Float32", (8, 6))
     mk.mm_naive(mk.get_backend(Am), (4, 2))(C2, Am, Bm, ndrange=(8, 6))
     np.testing.assert_array_equal(mk.Array(C2), mk.Array(Cm))
+
+
+@pytest.mark.parametrize("mode", ["0", "1"])
+def test_sgemm_shapes_with_each_kernel(cuda, mode):
+    """The shape tests again with the kernel forced: MK_SGEMM_PAIR=1 runs every
+    shape (ragged, split-K, K % 16) on CTA pairs, =0 on single CTAs; the
+    automatic choice picks one of the two by problem size."""
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, MK_SGEMM_PAIR=mode)
+    r = subprocess.run([sys.executable, "-m", "pytest", __file__, "-m", "gpu", "-q", "-x", "-p", "no:cacheprovider",
+                        "-k", "vs_fp64 or leading or golden or below_16 or keeps_bits"],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+
