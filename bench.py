@@ -19,6 +19,7 @@ rank 0 alone runs it.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import math
 import operator
@@ -116,6 +117,74 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+# ------------------------------------------------------------ configs -----
+
+# The five BASELINE configurations in the order the default run times them;
+# the mapreduce, the configuration the headline metric is quoted on, is last.
+BASELINE_KINDS = ["vadd", "gather", "histogram", "matmul", "reduce"]
+
+_WORKLOAD_TEXT = {
+    "reduce": ("mapreduce sum(x.^2), Float32 x ~ U[-1,1), n=2^28 per GPU (configs[1]), rel 1e-5 of fp64; "
+               "N>1: one global sum over all ranks' shards per step",
+               "input (1 GiB) larger than L2; no flush"),
+    "maximum": ("maximum(x) via mapreducedim!, Float32 x ~ U[-1,1), n=2^28 per GPU (scope row f1); Julia max "
+                "semantics, exact", "input (1 GiB) larger than L2; no flush"),
+    "findmax": ("findmax(x) (value, first 1-based index), Float32 x ~ U[-1,1), n=2^28 per GPU (scope row f1); "
+                "Julia order: NaN wins, +0 above -0, first index", "input (1 GiB) larger than L2; no flush"),
+    "vadd": ("vadd c=a+b Float32 n=2^20 per GPU (configs[0])", "L2 flushed (256 MiB read) before every launch"),
+    "gather": ("gather c=a[idx] Float32 a 2^27 (replicated on every GPU), Int32 idx 2^27 per GPU uniform in "
+               "[1,2^27] (configs[2])", "inputs (1.5 GiB) larger than L2; no flush"),
+    "gather_ceiling": ("random 4-byte reads of a 2^27 Float32 array at hashed positions, 2^27 per GPU, no index "
+                       "stream, one u32 checksum per block (device random-read ceiling for configs[2])",
+                       "array (512 MiB) larger than L2; no flush"),
+    "histogram": ("histogram Int32 keys 2^26 per GPU ~ Zipf(1.1) on 1..4096, UInt32 counts (configs[3]); counts "
+                  "zeroed each step; N>1: global counts over all ranks' keys per step",
+                  "input (256 MiB) larger than L2; no flush"),
+    "matmul": ("mm_tiled! C=A*B Float32 8192^3 per GPU (configs[4]), fp32 result within rel 1e-5 of fp64; "
+               "N>1: rank r owns row block r of an (8192N)x8192 A, B replicated", "operands larger than L2"),
+    "matmul_simt": ("mm_tiled! 16x16 SIMT, Float32 8192^3 per GPU (configs[4])", "operands larger than L2"),
+    "scan": ("cumsum of Float32 x ~ U[0,1), n=2^28 per GPU (scope row f2: AK.accumulate!)",
+             "input (1 GiB) larger than L2; no flush"),
+    "reduce_dims": ("sum(m; dims=1) of a 16384x16384 Float32 matrix per GPU (scope row f1: dims reductions)",
+                    "input (1 GiB) larger than L2; no flush"),
+}
+
+
+# How this library computes each workload (printed as "impl_notes" on its own
+# lines only; the reference arm computes the same workload its own way).
+IMPL_NOTES = {
+    "reduce": "fused single pass, fp64 accumulation; N>1: fp64 partials exchanged over NVLink peer memory "
+              "inside the same kernel, no NCCL call",
+    "matmul": "tcgen05 3xTF32 (TMEM accumulators, TMA-fed, CTA pairs); the split pre-pass is inside the step",
+    "histogram": "per-block shared-memory bins, flushed with global atomics; N>1: one NCCL all-reduce of 4096 u32",
+    "gather": "16-byte index/output streams, 8 random 4-byte loads in flight per thread",
+    "vadd": "16-byte loads/stores, grid of resident blocks",
+}
+
+
+def config_of(kind: str, world: int, n_override: int | None = None) -> dict:
+    """The ``config`` object of a kernel's JSON line.  Both arms print the same
+    one for the same N, so a run pair compares like with like."""
+    from cutilecpu_b200 import workloads
+    text, l2 = _WORKLOAD_TEXT[kind]
+    c: dict = {"workload": text}
+    base = workloads.CONFIGS
+    if kind in ("matmul", "matmul_simt"):
+        m = n_override or base["matmul"]["m"]
+        c.update(m=m, n=n_override or base["matmul"]["n"], k=n_override or base["matmul"]["k"])
+    elif kind == "reduce_dims":
+        r = n_override or (1 << 14)
+        c.update(rows=r, cols=r)
+    else:
+        src = {"maximum": "reduce", "findmax": "reduce", "gather_ceiling": "gather", "scan": None}.get(kind, kind)
+        c["n_per_gpu"] = n_override or (base[src]["n"] if src else 1 << 28)
+    c["l2"] = l2
+    c["parallelism"] = f"dp{world} (contiguous shards)" if world > 1 else "single GPU"
+    if n_override:
+        c["workload"] = "REDUCED SIZE (profiling case, not a benchmark line): " + c["workload"]
+    return c
+
+
 # ----------------------------------------------------------- workloads -----
 
 class Workload:
@@ -151,6 +220,35 @@ def _dist_allreduce_max(x: float) -> float:
     return x
 
 
+class CheckFailed(AssertionError):
+    """A benchmarked configuration's result differs from the oracle."""
+
+
+def dev_sms() -> int:
+    import torch
+    return torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+
+
+def _dist_sum_f64(x: float) -> float:
+    import torch
+    import torch.distributed as dist
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return t.item()
+    return x
+
+
+def _dist_sum_i64(a: np.ndarray) -> np.ndarray:
+    import torch
+    import torch.distributed as dist
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        t = torch.from_numpy(np.ascontiguousarray(a, dtype=np.int64)).cuda()
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return t.cpu().numpy()
+    return a
+
+
 def make_workload(kind: str, rank: int, world: int, n_override: int | None = None):
     import torch
 
@@ -175,10 +273,6 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             self.peer = distributed.PeerReduce() if world > 1 else None
             self.units_per_step = 4.0 * n
             self.h2d_bytes, self.d2h_bytes = 4 * n, 8
-            self.config = {"workload": "mapreduce sum(x.^2), Float32 x ~ U[-1,1), n=2^28 per GPU "
-                                       "(configs[1]); fused single pass, fp64 accumulation; N>1: partials "
-                                       "exchanged over NVLink peer memory inside the same kernel",
-                           "n_per_gpu": n, "l2": "input (1 GiB) larger than L2; no flush"}
 
         def launch(self):
             if self.peer is not None:  # fused: local reduction + NVLink exchange in one launch
@@ -191,11 +285,15 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             pass  # the exchange is inside the kernel
 
         def check(self):
+            # every N: the fused result against the fp64 oracle of all shards,
+            # and the same bits on every rank
             import oracle
             got = self.out.item()
-            if world == 1:
-                want = oracle.sum_sq(self.x_host)
-                assert abs(got - want) <= 1e-5 * abs(want), (got, want)
+            want = _dist_sum_f64(oracle.sum_sq(self.x_host))
+            if not abs(got - want) <= 1e-5 * abs(want):
+                raise CheckFailed(f"reduce: rank {rank} got {got!r}, oracle {want!r}")
+            if _dist_allreduce_max(got) != -_dist_allreduce_max(-got):
+                raise CheckFailed(f"reduce: ranks disagree (rank {rank} has {got!r})")
 
         def e2e_setup(self):
             self.pinned = torch.from_numpy(self.x_host).pin_memory()
@@ -229,9 +327,6 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             self.out = torch.empty(1, dtype=torch.float64, device="cuda")
             self.units_per_step = 4.0 * n
             self.h2d_bytes, self.d2h_bytes = 4 * n, 8
-            self.config = {"workload": "maximum(x) via mapreducedim!, Float32 x ~ U[-1,1), n=2^28 per GPU "
-                                       "(scope row f1); Julia max semantics, exact", "n_per_gpu": n,
-                           "l2": "input (1 GiB) larger than L2; no flush"}
 
         def launch(self):
             _lib.check(L.mk_mapreduce_f32(self.out.data_ptr(), self.x.pointer(), self.n, 0, 1, float("-inf"),
@@ -273,9 +368,6 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             self.idx = torch.empty(1, dtype=torch.int64, device="cuda")
             self.units_per_step = 4.0 * n
             self.h2d_bytes, self.d2h_bytes = 4 * n, 16
-            self.config = {"workload": "findmax(x) (value, first 1-based index), Float32 x ~ U[-1,1), n=2^28 per "
-                                       "GPU (scope row f1); Julia order: NaN wins, +0 above -0, first index",
-                           "n_per_gpu": n, "l2": "input (1 GiB) larger than L2; no flush"}
 
         def launch(self):
             _lib.check(L.mk_findext_f32(self.val.data_ptr(), self.idx.data_ptr(), self.x.pointer(), self.n, 1,
@@ -319,8 +411,6 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             self.c = mk.zeros(be, "Float32", n)
             self.units_per_step = 12.0 * n
             self.h2d_bytes, self.d2h_bytes = 8 * n, 4 * n
-            self.config = {"workload": "vadd c=a+b Float32 n=2^20 per GPU (configs[0])", "n_per_gpu": n,
-                           "l2": "L2 flushed (256 MiB read) before every launch"}
 
         def launch(self):
             _lib.check(L.mk_vadd_f32(self.c.pointer(), self.a.pointer(), self.b.pointer(), self.n, stream()),
@@ -330,7 +420,8 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             pass
 
         def check(self):
-            np.testing.assert_array_equal(mk.Array(self.c), self.a_host + self.b_host)
+            if not np.array_equal(mk.Array(self.c), self.a_host + self.b_host):
+                raise CheckFailed(f"vadd: rank {rank} differs from a+b")
 
         def e2e_setup(self):
             self.pa = torch.from_numpy(self.a_host).pin_memory()
@@ -367,9 +458,6 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             self.c = mk.zeros(be, "Float32", n)
             self.units_per_step = 12.0 * n
             self.h2d_bytes, self.d2h_bytes = 4 * n, 4 * n
-            self.config = {"workload": "gather c=a[idx] Float32 a 2^27 (replicated), Int32 idx 2^27 per GPU "
-                                       "uniform in [1,2^27] (configs[2])", "n_per_gpu": n,
-                           "l2": "inputs (1.5 GiB) larger than L2; no flush"}
 
         def launch(self):
             _lib.check(L.mk_gather_f32(self.c.pointer(), self.a.pointer(), self.na, self.idx.pointer(), self.n,
@@ -380,7 +468,33 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
 
         def check(self):
             got = mk.Array(self.c)
-            np.testing.assert_array_equal(got, self.a_host[self.idx_host.astype(np.int64) - 1])
+            if not np.array_equal(got, self.a_host[self.idx_host.astype(np.int64) - 1]):
+                raise CheckFailed(f"gather: rank {rank} differs from a[idx]")
+
+        def extra_roofline(self, K, kern_ms):
+            """This GPU's random-read ceiling for the same array and count:
+            mk_probe_random_read_f32 (no index or output stream), timed like
+            the kernel.  The gather's time over the probe's is its fraction of
+            what random 4-byte reads of `a` allow."""
+            sums = torch.empty(dev_sms() * 8, dtype=torch.int32, device="cuda")
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * K)]
+            for _ in range(3):
+                _lib.check(L.mk_probe_random_read_f32(sums.data_ptr(), sums.numel(), self.a.pointer(), self.na,
+                                                      self.n, 7, stream()), "probe")
+            for i in range(K):
+                ev[2 * i].record()
+                _lib.check(L.mk_probe_random_read_f32(sums.data_ptr(), sums.numel(), self.a.pointer(), self.na,
+                                                      self.n, 7 + i, stream()), "probe")
+                ev[2 * i + 1].record()
+            torch.cuda.synchronize()
+            probe_ms = _dist_allreduce_max(sum(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(K)) / K)
+            return {"random_ceiling": {
+                "probe": "mk_probe_random_read_f32: n random 4-byte .cg reads of the same 2^27-float array, "
+                         "no index/output streams",
+                "probe_ms": round(probe_ms, 5),
+                "reads_per_s": round(self.n / (probe_ms * 1e-3), 1),
+                "gather_equiv_gbs": round(12.0 * self.n / (probe_ms * 1e-3) / 1e9, 1),
+                "frac": round(probe_ms / kern_ms, 4)}}
 
         def e2e_setup(self):
             self.pidx = torch.from_numpy(self.idx_host).pin_memory()
@@ -401,6 +515,57 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
                                                self.idx_host.ctypes.data, self.n, 256), \
                 self.units_per_step, "full 2^27 gather, W=256"
 
+    class GatherCeiling(Workload):
+        name = "gather_ceiling"
+        metric = "random 4-byte reads of a 512 MiB array, GB/s (4 B per read)"
+        cfg = workloads.CONFIGS["gather"]
+
+        def __init__(self):
+            super().__init__(rank, world)
+            self.n, self.na = n_override or self.cfg["n"], self.cfg["na"]
+            self.a_host = workloads.uniform01(self.na, stream=20)
+            self.a = mk.MLIRArray(self.a_host)
+            self.sums = torch.empty(dev_sms() * 8, dtype=torch.int32, device="cuda")
+            self.units_per_step = 4.0 * self.n
+            self.h2d_bytes, self.d2h_bytes = 0, 4 * self.sums.numel()
+
+        def launch(self):
+            _lib.check(L.mk_probe_random_read_f32(self.sums.data_ptr(), self.sums.numel(), self.a.pointer(),
+                                                  self.na, self.n, 7, stream()), "probe")
+
+        def combine(self):
+            pass
+
+        def check(self):
+            # XOR of every word read, recomputed on the host with the same hash
+            i = np.arange(self.n, dtype=np.uint64)
+            h = (i.astype(np.uint32) ^ np.uint32(7)).astype(np.uint64)
+            for sh, mul in ((16, 0x85EBCA6B), (13, 0xC2B2AE35), (16, None)):
+                h ^= h >> np.uint64(sh)
+                if mul is not None:
+                    h = (h * np.uint64(mul)) & np.uint64(0xFFFFFFFF)
+            pos = (h * np.uint64(self.na)) >> np.uint64(32)
+            want = np.bitwise_xor.reduce(self.a_host.view(np.uint32)[pos])
+            got = np.bitwise_xor.reduce(self.sums.cpu().numpy().view(np.uint32))
+            if got != want:
+                raise CheckFailed(f"gather_ceiling: XOR {got:#x}, host {want:#x}")
+
+        def e2e_setup(self):
+            pass
+
+        def e2e_step(self):
+            self.launch()
+            return self.sums.cpu()
+
+        def cpu_sample(self, threads):
+            import oracle
+            Lo = oracle.lib()
+            c = np.empty(self.n, dtype=np.float32)
+            idx = workloads.indices1(self.n, self.na, stream=21)
+            return lambda: Lo.mlirb_gather_f32(c.ctypes.data, self.a_host.ctypes.data, self.na,
+                                               idx.ctypes.data, self.n, 256), \
+                4.0 * self.n, "the 2^27 CPU gather's random reads (4 B per read), W=256"
+
     class Scan(Workload):
         name = "scan"
         metric = "accumulate!(+) / cumsum HBM GB/s (8 B/element)"
@@ -414,8 +579,6 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             self.y = mk.zeros(be, "Float32", n)
             self.units_per_step = 8.0 * n
             self.h2d_bytes, self.d2h_bytes = 4 * n, 4 * n
-            self.config = {"workload": "cumsum of Float32 x ~ U[0,1), n=2^28 per GPU (scope row f2: AK.accumulate!)",
-                           "n_per_gpu": n, "l2": "input (1 GiB) larger than L2; no flush"}
 
         def launch(self):
             _lib.check(L.mk_accumulate_f32(self.y.pointer(), self.x.pointer(), self.n, 0, 0.0, 0, stream()), "scan")
@@ -460,9 +623,6 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             self.out = mk.zeros(be, "Float32", (1, r))
             self.units_per_step = 4.0 * r * r
             self.h2d_bytes, self.d2h_bytes = 4 * r * r, 4 * r
-            self.config = {"workload": "sum(m; dims=1) of a 16384x16384 Float32 matrix per GPU "
-                                       "(scope row f1: dims reductions)", "rows": r, "cols": r,
-                           "l2": "input (1 GiB) larger than L2; no flush"}
 
         def launch(self):
             _lib.check(L.mk_mapreduce_dim_f32(self.out.pointer(), self.m.pointer(), 1, self.r, self.c, 0, 0, 0.0,
@@ -507,9 +667,6 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             self.counts = mk.zeros(be, "UInt32", nb)
             self.units_per_step = 4.0 * n
             self.h2d_bytes, self.d2h_bytes = 4 * n, 4 * nb
-            self.config = {"workload": "histogram Int32 keys 2^26 per GPU ~ Zipf(1.1) on 1..4096, UInt32 counts "
-                                       "(configs[3]); counts zeroed each step", "n_per_gpu": n,
-                           "l2": "input (256 MiB) larger than L2; no flush"}
 
         def prepare(self):
             self.counts.storage.zero_()  # bins accumulate: every step starts from zero
@@ -522,9 +679,15 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             distributed.combine_counts(self.counts.storage)
 
         def check(self):
-            if world == 1:
-                import oracle
-                np.testing.assert_array_equal(mk.Array(self.counts), oracle.hist(self.keys_host, self.nb)[0])
+            # every N: the combined counts equal the oracle's counts of all
+            # ranks' keys, summed mod 2^32 (u32 wrap-around)
+            import oracle
+            mine = oracle.hist(self.keys_host, self.nb)[0].astype(np.int64)
+            want = (_dist_sum_i64(mine) % (1 << 32)).astype(np.uint32)
+            got = mk.Array(self.counts)
+            if not np.array_equal(got, want):
+                bad = int(np.flatnonzero(got != want)[0])
+                raise CheckFailed(f"histogram: rank {rank} bin {bad + 1} has {got[bad]}, oracle {want[bad]}")
 
         def e2e_setup(self):
             self.pk = torch.from_numpy(self.keys_host).pin_memory()
@@ -543,13 +706,12 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             import oracle
             Lo = oracle.lib()
             counts = np.zeros(self.nb, dtype=np.uint32)
-            m = (1 << 24)
-            return lambda: Lo.mlirb_hist_u32(counts.ctypes.data, self.nb, self.keys_host.ctypes.data, m, 256), \
-                4.0 * m, "first 2^24 of the 2^26 Zipf keys, per-lane atomics, W=256"
+            return lambda: Lo.mlirb_hist_u32(counts.ctypes.data, self.nb, self.keys_host.ctypes.data, self.n, 256), \
+                4.0 * self.n, "all 2^26 Zipf keys, per-lane atomics, W=256"
 
     class MatmulSimt(Workload):
         name = "matmul_simt"
-        metric = "matmul TFLOP/s (reference 16x16 SIMT algorithm)"
+        metric = "matmul C=A*B TFLOP/s (16x16 SIMT kernel)"
         unit = "TFLOP/s"
         cfg = workloads.CONFIGS["matmul"]
 
@@ -563,8 +725,6 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             self.C = mk.zeros(be, "Float32", (m, n))
             self.units_per_step = 2.0 * m * n * k
             self.h2d_bytes, self.d2h_bytes = 4 * (m * k + k * n), 4 * m * n
-            self.config = {"workload": "mm_tiled! 16x16 SIMT, Float32 8192^3 row block per GPU (configs[4])",
-                           "m": m, "n": n, "k": k, "l2": "operands larger than L2"}
 
         def launch(self):
             _lib.check(L.mk_matmul_tiled16_f32(self.C.pointer(), self.A.pointer(), self.B.pointer(), self.m, self.nn,
@@ -597,14 +757,14 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             import oracle
             Lo = oracle.lib()
             Cs = np.zeros((self.m, self.nn), dtype=np.float32, order="F")
-            cols = 64
+            cols = 512
             return lambda: Lo.mlirb_mm_tiled16_f32(Cs.ctypes.data, self.A_host.ctypes.data, self.B_host.ctypes.data,
                                                    self.m, self.nn, self.k, self.m, self.k, self.m, 0, cols), \
                 2.0 * self.m * cols * self.k, f"C[:, 1:{cols}] of the 8192^3 product (restated 16x16 tiles)"
 
     class Matmul(Workload):
         name = "matmul"
-        metric = "matmul TFLOP/s (3xTF32 on tcgen05 tensor cores)"
+        metric = "matmul C=A*B TFLOP/s"
         launches_per_step = 3  # split_a, split_b, sgemm_tf32x3
         unit = "TFLOP/s"
         cfg = workloads.CONFIGS["matmul"]
@@ -619,8 +779,6 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             self.C = mk.zeros(be, "Float32", (m, n))
             self.units_per_step = 2.0 * m * n * k
             self.h2d_bytes, self.d2h_bytes = 4 * (m * k + k * n), 4 * m * n
-            self.config = {"workload": "mm_tiled! C=A*B Float32 8192^3 per GPU (configs[4]); tcgen05 3xTF32, split pre-pass included",
-                           "m": m, "n": n, "k": k, "l2": "operands larger than L2"}
 
         def launch(self):
             _lib.check(L.mk_sgemm_3xtf32(self.C.pointer(), self.A.pointer(), self.B.pointer(), self.m, self.nn,
@@ -630,11 +788,20 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             pass
 
         def check(self):
+            # this rank's row block: C*v against A*(B*v) in fp64 (rel 1e-5, the
+            # configuration's tolerance) and sampled entries against fp64 dots
             import oracle
+            Cm = mk.Array(self.C)
+            v = np.random.Generator(np.random.Philox(9 + rank)).standard_normal(self.nn)
+            want = oracle.matvec_chain_f64(self.A_host, self.B_host, v)
+            err = np.linalg.norm(oracle.matvec_f64(Cm, v) - want) / np.linalg.norm(want)
+            if not err <= 1e-5:
+                raise CheckFailed(f"matmul: rank {rank} rel error of C*v {err:.3e} > 1e-5")
             ii = np.array([0, 1, self.m // 2, self.m - 1]); jj = np.array([0, self.nn - 1, 17, self.nn // 2])
-            got = mk.Array(self.C)[ii, jj]
+            got = Cm[ii, jj]
             want = oracle.matmul_entries_f64(self.A_host, self.B_host, ii, jj)
-            np.testing.assert_allclose(got, want, rtol=1e-4, atol=2e-4)
+            if not np.allclose(got, want, rtol=1e-4, atol=2e-4):
+                raise CheckFailed(f"matmul: rank {rank} sampled entries {got} vs {want}")
 
         def e2e_setup(self):
             self.pA = torch.from_numpy(self.A_host.ravel(order="F")).pin_memory()
@@ -653,12 +820,13 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             import oracle
             Lo = oracle.lib()
             Cs = np.zeros((self.m, self.nn), dtype=np.float32, order="F")
-            cols = 64
+            cols = 512
             return lambda: Lo.mlirb_mm_tiled16_f32(Cs.ctypes.data, self.A_host.ctypes.data, self.B_host.ctypes.data,
                                                    self.m, self.nn, self.k, self.m, self.k, self.m, 0, cols), \
                 2.0 * self.m * cols * self.k, f"C[:, 1:{cols}] of the 8192^3 product (restated 16x16 tiles)"
 
     table = {"reduce": Reduce, "maximum": Maximum, "findmax": FindMax, "vadd": Vadd, "gather": Gather,
+             "gather_ceiling": GatherCeiling,
              "histogram": Histogram,
              "matmul": Matmul, "matmul_simt": MatmulSimt,
              "scan": Scan, "reduce_dims": Dims}
@@ -765,6 +933,8 @@ def run_ours(kind: str, args, rank: int, world: int, local_rank: int) -> dict | 
                "cores": oracle.num_threads(), "kind": "port",
                "sample": f"{sample}; restated MLIRBackend (oracle/oracle.c), median of {reps} reps"}
 
+    # collective on every rank (max over ranks), so before rank 0 goes on alone
+    extra = w.extra_roofline(K, kern_avg_max) if hasattr(w, "extra_roofline") else {}
     if rank != 0:
         return None
     scale = 1e12 if w.unit == "TFLOP/s" else 1e9
@@ -783,12 +953,14 @@ def run_ours(kind: str, args, rank: int, world: int, local_rank: int) -> dict | 
     else:
         roof = {"bound": "simt-fp32", "achieved": round(achieved, 2), "peak": None, "unit": "TFLOP/s",
                 "frac": None, "traffic": None}
+    roof.update(extra)
     line = {
         "metric": w.metric, "value": round(total_units / (step_ms * 1e-3) / scale, 2), "unit": w.unit,
         "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": round(step_ms, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
         "data": "synthetic (seeded numpy Philox, host-generated)",
-        "config": dict(w.config, parallelism=f"dp{world} (contiguous shards)" if world > 1 else "single GPU"),
+        "config": config_of(kind, world, args.n),
+        "impl_notes": IMPL_NOTES.get(kind),
         "e2e": {"value": round(total_units / (e2e_ms * 1e-3) / scale, 3), "unit": w.unit,
                 "h2d_bytes_per_step": w.h2d_bytes, "d2h_bytes_per_step": w.d2h_bytes},
         "gpu_launches": K * w.launches_per_step,
@@ -842,30 +1014,27 @@ def run_reference(kind: str, args, world: int = 1) -> dict:
         fn = lambda: L.mlirb_sum_sq_f32(x.ctypes.data, n, 256, tmp.ctypes.data)  # noqa: E731
         units, unit, metric = 4.0 * n, "GB/s", "mapreduce sum(x.^2) HBM GB/s"
         sample = "full 2^28-element sum(x.^2) per step"
-        conf = "mapreduce sum(x.^2), Float32 x ~ U[-1,1), n=2^28 (configs[1])"
     elif kind == "vadd":
         n = cfg["vadd"]["n"]
         a, b = workloads.uniform01(n, stream=10), workloads.uniform01(n, stream=11)
         c = np.empty_like(a)
         fn = lambda: L.mlirb_vadd_f32(c.ctypes.data, a.ctypes.data, b.ctypes.data, n, 256)  # noqa: E731
         units, unit, metric = 12.0 * n, "GB/s", "vadd HBM GB/s"
-        sample, conf = "full n=2^20 vadd per step", "vadd c=a+b Float32 n=2^20 (configs[0])"
+        sample = "full n=2^20 vadd per step"
     elif kind == "gather":
         n, na = cfg["gather"]["n"], cfg["gather"]["na"]
         a, idx = workloads.uniform01(na, stream=20), workloads.indices1(n, na, stream=21)
         c = np.empty(n, dtype=np.float32)
         fn = lambda: L.mlirb_gather_f32(c.ctypes.data, a.ctypes.data, na, idx.ctypes.data, n, 256)  # noqa: E731
         units, unit, metric = 12.0 * n, "GB/s", "indirect gather HBM GB/s (algorithmic 12 B/elem)"
-        sample, conf = "full 2^27 gather per step", "gather Float32 a 2^27, Int32 idx 2^27 (configs[2])"
+        sample = "full 2^27 gather per step"
     elif kind == "histogram":
         n, nb = cfg["histogram"]["n"], cfg["histogram"]["nbins"]
         keys = workloads.zipf_keys(n, nb, 1.1, stream=30)
         counts = np.zeros(nb, dtype=np.uint32)
-        m = 1 << 24
-        fn = lambda: L.mlirb_hist_u32(counts.ctypes.data, nb, keys.ctypes.data, m, 256)  # noqa: E731
-        units, unit, metric = 4.0 * m, "GB/s", "histogram HBM GB/s (4 B/key)"
-        sample = "first 2^24 of the 2^26 Zipf keys per step"
-        conf = "histogram Int32 keys ~ Zipf(1.1) on 1..4096 (configs[3])"
+        fn = lambda: L.mlirb_hist_u32(counts.ctypes.data, nb, keys.ctypes.data, n, 256)  # noqa: E731
+        units, unit, metric = 4.0 * n, "GB/s", "histogram HBM GB/s (4 B/key)"
+        sample = "all 2^26 Zipf keys per step"
     elif kind == "scan":
         n = 1 << 28
         x = workloads.uniform01(n, stream=50)
@@ -873,25 +1042,27 @@ def run_reference(kind: str, args, world: int = 1) -> dict:
         tot = np.empty(n // 512 + 2, dtype=np.float32)
         fn = lambda: L.mlirb_cumsum_f32(out.ctypes.data, x.ctypes.data, n, 256, tot.ctypes.data)  # noqa: E731
         units, unit, metric = 8.0 * n, "GB/s", "accumulate!(+) / cumsum HBM GB/s (8 B/element)"
-        sample, conf = "full 2^28 cumsum per step", "cumsum Float32 n=2^28"
+        sample = "full 2^28 cumsum per step"
     elif kind == "reduce_dims":
         r = 1 << 14
         m = workloads.uniform01(r * r, stream=60)
         out = np.empty(r, dtype=np.float32)
         fn = lambda: L.mlirb_sum_dims1_f32(out.ctypes.data, m.ctypes.data, r, r)  # noqa: E731
         units, unit, metric = 4.0 * r * r, "GB/s", "sum(m; dims=1) HBM GB/s (4 B/element)"
-        sample, conf = "full 16384x16384 sum(m; dims=1) per step", "sum(m; dims=1) Float32 16384x16384"
-    else:
+        sample = "full 16384x16384 sum(m; dims=1) per step"
+    elif kind in ("matmul", "matmul_simt"):
         m = cfg["matmul"]["m"]
         A = workloads.normal((m, m), stream=40)
         B = workloads.normal((m, m), stream=41)
         Cs = np.zeros((m, m), dtype=np.float32, order="F")
-        cols = 64
+        cols = 512
         fn = lambda: L.mlirb_mm_tiled16_f32(Cs.ctypes.data, A.ctypes.data, B.ctypes.data, m, m, m, m, m, m,  # noqa
                                             0, cols)
-        units, unit, metric = 2.0 * m * cols * m, "TFLOP/s", "matmul TFLOP/s (reference 16x16 SIMT algorithm)"
+        units, unit = 2.0 * m * cols * m, "TFLOP/s"
+        metric = "matmul C=A*B TFLOP/s" + (" (16x16 SIMT kernel)" if kind == "matmul_simt" else "")
         sample = f"C[:, 1:{cols}] of the 8192^3 product per step"
-        conf = "mm_tiled! Float32 8192^3 (configs[4])"
+    else:
+        raise SystemExit(f"--impl reference: no CPU restatement of --kernel {kind}")
     for _ in range(args.warmup):
         fn()
     t0 = time.perf_counter()
@@ -903,7 +1074,7 @@ def run_reference(kind: str, args, world: int = 1) -> dict:
     return {"metric": metric, "value": v, "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded numpy Philox, host-generated)", "impl": "reference",
-            "config": {"workload": conf, "parallelism": "host OpenMP"},
+            "config": config_of(kind, world, None),
             "cpu_baseline": {"value": v, "unit": unit, "cores": threads, "kind": "port",
                              "sample": sample + "; restated MLIRBackend (oracle/oracle.c); the Julia reference "
                                                 "cannot run here (no julia)"},
@@ -916,18 +1087,22 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--kernel", default="reduce",
-                    choices=["reduce", "maximum", "findmax", "vadd", "gather", "histogram", "matmul", "matmul_simt",
-                             "scan", "reduce_dims", "all"])
+    ap.add_argument("--kernel", default="baseline",
+                    choices=["baseline", "reduce", "maximum", "findmax", "vadd", "gather", "gather_ceiling",
+                             "histogram", "matmul", "matmul_simt", "scan", "reduce_dims", "all"],
+                    help="baseline (default): the five BASELINE configurations, mapreduce last")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--n", type=int, default=None,
                     help="override the element count of the configuration (small profiling cases)")
     args = ap.parse_args()
-    kinds = (["reduce", "maximum", "findmax", "vadd", "gather", "histogram", "matmul", "matmul_simt", "scan",
-              "reduce_dims"]
-             if args.kernel == "all" else [args.kernel])
+    if args.kernel == "baseline":
+        kinds = list(BASELINE_KINDS)
+    elif args.kernel == "all":
+        kinds = ["maximum", "findmax", "gather_ceiling", "matmul_simt", "scan", "reduce_dims"] + BASELINE_KINDS
+    else:
+        kinds = [args.kernel]
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -949,16 +1124,23 @@ def main():
     if world > 1:
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
-    defaults = {"reduce": (2000, 50), "maximum": (1000, 20), "findmax": (1000, 20), "vadd": (2000, 50), "gather": (200, 10), "histogram": (500, 20),
-                "matmul": (20, 3), "matmul_simt": (3, 1), "scan": (500, 20), "reduce_dims": (1000, 20)}
+    defaults = {"reduce": (2000, 50), "maximum": (1000, 20), "findmax": (1000, 20), "vadd": (2000, 50),
+                "gather": (200, 10), "gather_ceiling": (200, 10), "histogram": (500, 20), "matmul": (20, 3),
+                "matmul_simt": (3, 1), "scan": (500, 20), "reduce_dims": (1000, 20)}
     try:
         for k in kinds:
             a = argparse.Namespace(**vars(args))
             a.steps = args.steps if args.steps is not None else defaults[k][0]
             a.warmup = max(3, args.warmup if args.warmup is not None else defaults[k][1])
-            line = run_ours(k, a, rank, world, local_rank)
+            try:
+                line = run_ours(k, a, rank, world, local_rank)
+            except CheckFailed as e:
+                print(f"bench.py: result check failed: {e}", file=sys.stderr, flush=True)
+                sys.exit(1)
             if line is not None:
                 print(json.dumps(line), flush=True)
+            gc.collect()
+            torch.cuda.empty_cache()
     finally:
         if world > 1:
             dist.destroy_process_group()

@@ -37,6 +37,7 @@ SIGNATURES = {
     "mk_accumulate_f32": (_int, [_vp, _vp, _i64, _int, _f64, _int, _vp]),
     "mk_findext_f32": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
     "mk_gather_f32": (_int, [_vp, _vp, _i64, _vp, _i64, _vp]),
+    "mk_probe_random_read_f32": (_int, [_vp, _i64, _vp, _i64, _i64, C.c_uint, _vp]),
     "mk_hist_u32": (_int, [_vp, _i32, _vp, _i64, _vp]),
     "mk_hist": (_int, [_vp, _int, _i32, _vp, _int, _i64, _vp]),
     "mk_sgemm_3xtf32": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),

@@ -114,3 +114,70 @@ extern "C" int mk_gather_f32(float* c, const float* a, int64_t na, const int32_t
   }
   return mk::check_launch("mk_gather_f32: launch");
 }
+
+// ---------------------------------------------------------------------------
+// Random-read probe: the device's ceiling for the gather's dominant cost.
+// n independent 4-byte reads of a[h(i) mod na] with h a 32-bit integer hash of
+// the element number, the same loads (.cg, 8 in flight per thread) and grid as
+// gather_f32_vec4, but no index stream and no output stream: what is left is
+// the random-read rate of this GPU's memory system for an array of na floats.
+// Each block writes one u32 (XOR of the bits it read) so no load is dead code.
+// ---------------------------------------------------------------------------
+namespace {
+
+// Integer finaliser of MurmurHash3 (Appleby, public domain): a bijection of
+// u32 with full avalanche, so consecutive i land on unrelated lines.
+__device__ __forceinline__ uint32_t mix32(uint32_t h) {
+  h ^= h >> 16;
+  h *= 0x85ebca6bu;
+  h ^= h >> 13;
+  h *= 0xc2b2ae35u;
+  h ^= h >> 16;
+  return h;
+}
+
+__global__ void __launch_bounds__(kThreads)
+random_read_probe(unsigned* __restrict__ sums, const float* __restrict__ a, uint64_t na, int64_t n, uint32_t seed) {
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  constexpr int kInFlight = 4 * kUnroll;
+  unsigned acc = 0;
+  for (; i + (kInFlight - 1) * stride < n; i += kInFlight * stride) {
+    float v[kInFlight];
+#pragma unroll
+    for (int u = 0; u < kInFlight; ++u) {
+      const uint32_t h = mix32((uint32_t)(i + u * stride) ^ seed);
+      v[u] = __ldcg(a + (uint64_t)(((uint64_t)h * na) >> 32));
+    }
+#pragma unroll
+    for (int u = 0; u < kInFlight; ++u) acc ^= __float_as_uint(v[u]);
+  }
+  for (; i < n; i += stride) acc ^= __float_as_uint(__ldcg(a + (((uint64_t)mix32((uint32_t)i ^ seed) * na) >> 32)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc ^= __shfl_xor_sync(0xffffffffu, acc, o);
+  __shared__ unsigned part[kThreads / 32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned r = 0;
+    for (int w = 0; w < kThreads / 32; ++w) r ^= part[w];
+    sums[blockIdx.x] = r;
+  }
+}
+
+}  // namespace
+
+extern "C" int mk_probe_random_read_f32(unsigned* sums, int64_t sums_len, const float* a, int64_t na, int64_t n,
+                                        unsigned seed, void* stream) {
+  MK_ENTRY_DEVICE(dev);
+  if (n < 0 || na <= 0 || na > (int64_t)UINT32_MAX)
+    return mk::fail(MK_ERR_INVALID, "mk_probe_random_read_f32: need n >= 0 and 0 < na < 2^32");
+  if (!sums || !a) return mk::fail(MK_ERR_INVALID, "mk_probe_random_read_f32: null pointer");
+  const int64_t blocks = (int64_t)dev->sms * (2048 / kThreads);
+  if (sums_len < blocks)
+    return mk::fail(MK_ERR_INVALID, "mk_probe_random_read_f32: sums must hold " + std::to_string(blocks) +
+                                        " values (SMs x 8)");
+  if (n == 0) return MK_OK;
+  random_read_probe<<<(unsigned)blocks, kThreads, 0, mk::as_stream(stream)>>>(sums, a, (uint64_t)na, n, seed);
+  return mk::check_launch("mk_probe_random_read_f32: launch");
+}

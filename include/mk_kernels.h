@@ -154,6 +154,15 @@ MK_API int mk_findext_f32(double* val_out, int64_t* idx_out, const float* x, int
 MK_API int mk_gather_f32(float* c, const float* a, int64_t na, const int32_t* idx1,
                   int64_t n, void* stream);
 
+/* Measurement probe with no counterpart in the reference: n independent
+ * 4-byte reads of a[0, na) at positions hashed from the element number, with
+ * the loads, grid and loads in flight of mk_gather_f32 but no index or output
+ * stream.  Its duration is this GPU's ceiling for the gather's random reads.
+ * sums receives one u32 (XOR of the bits read) per block: SMs x 8 values,
+ * sums_len must be at least that.  seed varies the positions. */
+MK_API int mk_probe_random_read_f32(unsigned* sums, int64_t sums_len, const float* a, int64_t na, int64_t n,
+                                    unsigned seed, void* stream);
+
 /* counts[keys1[i] - 1] += 1 for i in [0, n), u32 wrap-around, ACCUMULATING into
  * the caller's counts (as `@atomic bins[idx[i]] += 1` does).  Keys outside
  * [1, nbins] are skipped and set the device error word.  Bit-exact.

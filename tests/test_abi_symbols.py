@@ -2,7 +2,7 @@
 include/*.h declares; the Python binding covers the same set."""
 import ctypes
 import re
-from pathlib import Path
+import subprocess
 
 from conftest import ROOT
 
@@ -41,6 +41,13 @@ def test_version_and_last_error_without_gpu():
 
 
 def test_library_has_no_oracle_dependency():
-    # the product library must not link or embed the CPU oracle
-    data = Path(_lib.LIB_PATH).read_bytes()
-    assert b"or_mapreduce_f64" not in data and b"mlirb_" not in data
+    # the product library neither exports nor links the CPU oracle: read its
+    # dynamic symbol table and its DT_NEEDED entries (names only)
+    syms = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], check=True,
+                          capture_output=True, text=True).stdout
+    names = {line.split()[-1] for line in syms.splitlines() if line.strip()}
+    assert not any(n.startswith(("or_", "mlirb_")) for n in names)
+    dyn = subprocess.run(["readelf", "-d", str(_lib.LIB_PATH)], check=True,
+                         capture_output=True, text=True).stdout
+    needed = re.findall(r"\(NEEDED\).*\[(.+?)\]", dyn)
+    assert needed and not any("oracle" in n for n in needed)

@@ -268,6 +268,18 @@ def test_hist_zipf_vs_oracle(L):
     np.testing.assert_array_equal(hist_dev(L, keys, 4096), oracle.hist(keys, 4096)[0])
 
 
+def test_hist_zipf_full_config_vs_oracle(L):
+    # BASELINE configs[3] at its full size: 2^26 Zipf(1.1) keys over 4096 bins,
+    # exact counts (the reference pins its KA histogram exactly,
+    # test/test_gpu_simt.jl:353-359)
+    from cutilecpu_b200 import workloads
+    keys = workloads.zipf_keys(1 << 26, 4096, 1.1, stream=30)
+    got = hist_dev(L, keys, 4096)
+    want = oracle.hist(keys, 4096)[0]
+    np.testing.assert_array_equal(got, want)
+    assert int(got.sum(dtype=np.int64)) == 1 << 26
+
+
 def test_hist_accumulates_and_wraps(L):
     start = np.zeros(16, dtype=np.uint32)
     start[0] = 0xFFFFFFFF

@@ -3,6 +3,8 @@ cumsum (test/test_downstream_ka.jl:39-42 inclusive of 1:n, :75-78 exclusive).
 Bar: each output within 1e-6 of the running sum of |x| (one Float32 rounding
 of an fp64 carry); max/min exact."""
 import operator
+import os
+import sys
 
 import numpy as np
 import pytest
@@ -95,3 +97,47 @@ def test_surface_accumulate_and_cumsum(cuda):
     ex = mk.zeros(mk.get_backend(src), "Float32", 1024)
     mk.accumulate(operator.add, ex, src, init=0.0, inclusive=False)
     np.testing.assert_array_equal(mk.Array(ex)[1:], mk.Array(dst)[:-1])
+
+
+_TIMEOUT_CHILD = r"""
+import sys
+import numpy as np, torch
+sys.path.insert(0, sys.argv[1])
+from cutilecpu_b200 import _lib
+L = _lib.lib()
+n = 1 << 26
+x = torch.rand(n, device="cuda")
+y = torch.empty_like(x)
+s = torch.cuda.current_stream().cuda_stream
+assert L.mk_accumulate_f32(y.data_ptr(), x.data_ptr(), n, 0, 0.0, 0, s) == 0, _lib.last_error()
+rc = L.mk_error_poll(s)
+print("POLL", rc, _lib.last_error())
+# the context stays usable after the timeout: a plain kernel still runs
+z = torch.ones(1024, device="cuda").sum().item()
+print("AFTER", z)
+"""
+
+
+def test_lookback_wait_runs_out_and_reports_timeout(cuda, tmp_path):
+    """The look-back wait is bounded: with a budget of one SM cycle
+    (MK_WAIT_LIMIT_CYCLES=1) the tiles that find a predecessor unpublished give
+    up, publish a prefix anyway (so no successor waits forever) and raise the
+    timeout bit, which mk_error_poll reports as MK_ERR_TIMEOUT, the library's
+    counterpart of the KernelException the reference raises for a device
+    error (test/test_gpu_simt.jl:497-565).  Runs in a child process because
+    the limit is read once per process; a fresh child then scans normally."""
+    import subprocess
+    from conftest import ROOT
+    script = tmp_path / "child.py"
+    script.write_text(_TIMEOUT_CHILD)
+    env = dict(os.environ, MK_WAIT_LIMIT_CYCLES="1")
+    r = subprocess.run([sys.executable, str(script), str(ROOT)], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    poll = [ln for ln in r.stdout.splitlines() if ln.startswith("POLL")][0].split()
+    assert int(poll[1]) == _lib.MK_ERR_TIMEOUT, r.stdout
+    assert "timed out" in r.stdout
+    assert "AFTER 1024.0" in r.stdout
+    # and without the tiny limit (this process, default budget) the same size is right
+    x = np.random.Generator(np.random.Philox(5)).random(1 << 26, dtype=np.float32)
+    check_add(scan(x), x)
