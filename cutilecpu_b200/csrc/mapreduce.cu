@@ -77,39 +77,6 @@ __device__ __forceinline__ double block_reduce(double v, double* smem) {
   return v;  // valid in thread 0
 }
 
-// Multi-GPU exchange (one thread): publish this rank's partial into every
-// rank's mailbox over NVLink, then wait (bounded) for every rank's partial of
-// this epoch and fold them in rank order, so all ranks get the same value.
-template <int OP>
-__device__ double exchange(double mine, const mk::PeerArgs& peer, unsigned* err) {
-  const int par = (int)(peer.epoch & 1ull);
-  for (int p = 0; p < peer.world; ++p)
-    asm volatile("st.relaxed.sys.global.f64 [%0], %1;" ::"l"(peer.slots[p] + par * MK_MAX_PEERS + peer.rank),
-                 "d"(mine)
-                 : "memory");
-  __threadfence_system();
-  for (int p = 0; p < peer.world; ++p)
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(peer.flags[p] + peer.rank), "l"(peer.epoch) : "memory");
-  const unsigned long long* my_flags = peer.flags[peer.rank];
-  const double* my_slots = peer.slots[peer.rank] + par * MK_MAX_PEERS;
-  const long long t0 = clock64();
-  double acc = neutral<OP>();
-  for (int q = 0; q < peer.world; ++q) {
-    unsigned long long f;
-    do {
-      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(f) : "l"(my_flags + q) : "memory");
-      if (f < peer.epoch && (unsigned long long)(clock64() - t0) > peer.limit) {
-        atomicOr(err, mk::ERRBIT_TIMEOUT);  // a rank never arrived: report, fold what is there
-        break;
-      }
-    } while (f < peer.epoch);
-    double v;
-    asm volatile("ld.relaxed.sys.global.f64 %0, [%1];" : "=d"(v) : "l"(my_slots + q) : "memory");
-    acc = combine<OP>(acc, v);
-  }
-  return acc;
-}
-
 // x: base pointer; the first `head` (0..3) elements precede the first 16-byte
 // boundary and are folded by the first `head` threads, like the <4 tail.
 template <int F, int OP>
@@ -180,9 +147,22 @@ mapreduce_kernel(const float* __restrict__ x, int64_t n, int head, double init,
   v = block_reduce<OP>(v, smem);
   if (threadIdx.x == 0) {
     *ticket = 0u;  // re-arm for the next reduction on this stream
-    if (peer.world > 0) v = exchange<OP>(v, peer, err);
-    out[0] = combine<OP>(init, v);
+    if (peer.world == 0) {
+      out[0] = combine<OP>(init, v);
+    } else {
+      // multi-GPU: publish this rank's partial, finish the previous pipelined
+      // call's global result (its partials have had a whole kernel to
+      // arrive), and in the blocking form wait for this call's own epoch
+      mk::peerdev::publish(v, peer);
+      mk::peerdev::complete_pending(peer, err);
+      if (peer.wait_own) out[0] = combine<OP>(init, mk::peerdev::fold(peer, peer.epoch, OP, err));
+    }
   }
+}
+
+// Completes the pending pipelined result of mk_mapreduce_f32_allreduce_async.
+__global__ void allreduce_complete_kernel(const mk::PeerArgs peer, unsigned* __restrict__ err) {
+  if (threadIdx.x == 0) mk::peerdev::complete_pending(peer, err);
 }
 
 // The grid is persistent: never more blocks than fit on the GPU at once (the
@@ -269,13 +249,45 @@ extern "C" int mk_mapreduce_f32(double* out_dev, const float* x, int64_t n, int 
   return mapreduce_impl(dev, out_dev, x, n, f, op, init, stream, mk::PeerArgs());
 }
 
-extern "C" int mk_mapreduce_f32_allreduce(double* out_dev, const float* x, int64_t n, int f, int op, double init,
-                                          void* stream) {
+namespace {
+
+int allreduce_entry(bool blocking, double* out_dev, const float* x, int64_t n, int f, int op, double init,
+                    void* stream) {
   MK_ENTRY_DEVICE(dev);
+  // argument errors before an epoch is taken, so a rejected call leaves the
+  // ranks' epoch counters in step
+  if (n < 0) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: n must be >= 0");
+  if (!out_dev || (n > 0 && !x)) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: null pointer");
+  if (f < MK_F_IDENTITY || f > MK_F_GT0) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: unknown f");
+  if (op < MK_OP_ADD || op > MK_OP_MUL) return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: unknown op");
+  if (n > 0 && (reinterpret_cast<uintptr_t>(x) & 3u) != 0)
+    return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: x must be 4-byte aligned");
   mk::PeerArgs peer;
-  int rc = mk::peer_args_next(dev, &peer);
+  int rc = mk::peer_args_next(dev, &peer, blocking, out_dev, op, init);
   if (rc != MK_OK) return rc;
   return mapreduce_impl(dev, out_dev, x, n, f, op, init, stream, peer);
+}
+
+}  // namespace
+
+extern "C" int mk_mapreduce_f32_allreduce(double* out_dev, const float* x, int64_t n, int f, int op, double init,
+                                          void* stream) {
+  return allreduce_entry(true, out_dev, x, n, f, op, init, stream);
+}
+
+extern "C" int mk_mapreduce_f32_allreduce_async(double* out_dev, const float* x, int64_t n, int f, int op,
+                                                double init, void* stream) {
+  return allreduce_entry(false, out_dev, x, n, f, op, init, stream);
+}
+
+extern "C" int mk_allreduce_complete(void* stream) {
+  MK_ENTRY_DEVICE(dev);
+  mk::PeerArgs peer;
+  bool pending = false;
+  int rc = mk::peer_args_complete(dev, &peer, &pending);
+  if (rc != MK_OK || !pending) return rc;
+  allreduce_complete_kernel<<<1, 32, 0, mk::as_stream(stream)>>>(peer, dev->err_word);
+  return mk::check_launch("mk_allreduce_complete: launch");
 }
 
 extern "C" int mk_sum_sq_f32(double* out_dev, const float* x, int64_t n, void* stream) {

@@ -19,6 +19,19 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
+// Complete `bytes` of the current phase's transaction count without a copy:
+// stands in for a copy that was never issued, so a drain can wait for a phase.
+__device__ __forceinline__ void mbar_complete_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Budget of the waits that make a kernel's exit safe after an abort (copies
+// and MMAs already issued must land before shared memory or TMEM is given
+// back).  Fixed, so a small MK_WAIT_LIMIT_CYCLES cannot cut a drain short:
+// 2^27 SM cycles is about 70 ms at 1.9 GHz, while an issued copy lands in
+// microseconds.
+constexpr unsigned long long kDrainCycles = 1ull << 27;
+
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }

@@ -2,9 +2,9 @@
 // GPU: each rank creates its mailbox, the host side exchanges the CUDA IPC
 // handles (torch.distributed all_gather in the Python layer), and every rank
 // maps the others' mailboxes.  Epochs start at 1 and only grow, so flags never
-// need resetting; a rank is at most one epoch ahead of any peer (it cannot
-// finish epoch e+1 without every peer's epoch-e+1 partial), which is why two
-// parity slots suffice.
+// need resetting; the slot ring of peer.cuh bounds how far ranks may drift.
+// The host keeps, per device, at most one pending pipelined result: the one
+// the next exchanging launch (or mk_allreduce_complete) writes.
 #include <cstring>
 #include <mutex>
 
@@ -19,6 +19,11 @@ struct Mailbox {
   bool opened[MK_MAX_PEERS] = {};
   unsigned long long epoch = 0;
   bool connected = false;
+  // pending pipelined result
+  unsigned long long pend_epoch = 0;
+  double* pend_out = nullptr;
+  int pend_op = 0;
+  double pend_init = 0.0;
 };
 
 std::mutex g_mu;
@@ -28,20 +33,60 @@ Mailbox g_box[64];
 
 namespace mk {
 
-int peer_args_next(Device* dev, PeerArgs* out) {
+namespace {
+
+void fill_common(const Mailbox& m, PeerArgs* a) {
+  a->world = m.world;
+  a->rank = m.rank;
+  a->limit = wait_limit_cycles();
+  for (int p = 0; p < m.world; ++p) {
+    char* base = static_cast<char*>(m.peers[p]);
+    a->slots[p] = reinterpret_cast<double*>(base);
+    a->flags[p] = reinterpret_cast<unsigned long long*>(base + kMailboxSlotsBytes);
+  }
+}
+
+void take_pending(Mailbox& m, PeerArgs* a) {
+  a->pend_epoch = m.pend_epoch;
+  a->pend_out = m.pend_out;
+  a->pend_op = m.pend_op;
+  a->pend_init = m.pend_init;
+  m.pend_epoch = 0;
+  m.pend_out = nullptr;
+}
+
+}  // namespace
+
+int peer_args_next(Device* dev, PeerArgs* out, bool blocking, double* res, int op, double init) {
   std::lock_guard<std::mutex> lk(g_mu);
   Mailbox& m = g_box[dev->id];
   if (!m.connected) return fail(MK_ERR_INVALID, "peer mailbox of this device is not connected (mk_peer_connect)");
   PeerArgs a;
-  a.world = m.world;
-  a.rank = m.rank;
+  fill_common(m, &a);
   a.epoch = ++m.epoch;
-  a.limit = wait_limit_cycles();
-  for (int p = 0; p < m.world; ++p) {
-    char* base = static_cast<char*>(m.peers[p]);
-    a.slots[p] = reinterpret_cast<double*>(base);
-    a.flags[p] = reinterpret_cast<unsigned long long*>(base + kMailboxSlotsBytes);
+  a.wait_own = blocking ? 1 : 0;
+  take_pending(m, &a);
+  if (!blocking) {
+    m.pend_epoch = a.epoch;
+    m.pend_out = res;
+    m.pend_op = op;
+    m.pend_init = init;
   }
+  *out = a;
+  return MK_OK;
+}
+
+int peer_args_complete(Device* dev, PeerArgs* out, bool* has_pending) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Mailbox& m = g_box[dev->id];
+  *has_pending = false;
+  if (!m.connected) return fail(MK_ERR_INVALID, "peer mailbox of this device is not connected (mk_peer_connect)");
+  if (m.pend_epoch == 0) return MK_OK;
+  PeerArgs a;
+  fill_common(m, &a);
+  a.epoch = 0;
+  take_pending(m, &a);
+  *has_pending = true;
   *out = a;
   return MK_OK;
 }

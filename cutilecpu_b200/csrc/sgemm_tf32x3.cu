@@ -304,11 +304,15 @@ sgemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
       if (!ok) {
         *abort_flag = 1;
         atomicOr(err, mk::ERRBIT_TIMEOUT);
-        // drain: the last (up to STAGES) copies may still be landing in smem
-        volatile int no_abort = 0;
-        for (int kb = issued - 1; kb >= 0 && kb >= issued - STAGES; --kb)
-          wait_bounded(full0 + 8 * (kb % STAGES), (kb / STAGES) & 1, limit, &no_abort);
       }
+      // Drain, whether or not anything aborted: the last (up to STAGES) copies
+      // may still be landing in shared memory if the MMA stopped consuming.
+      // Every earlier stage was consumed (its slot was freed before reuse), so
+      // only this window can be in flight.  On the normal path each of these
+      // phases has completed and the waits return at once.
+      volatile int no_abort = 0;
+      for (int kb = issued - 1; kb >= 0 && kb >= issued - STAGES; --kb)
+        wait_bounded(full0 + 8 * (kb % STAGES), (kb / STAGES) & 1, kDrainCycles, &no_abort);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -404,7 +408,7 @@ sgemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
   if (warp == 2) {
     // every issued MMA has completed before the columns are released
     volatile int no_abort = 0;
-    wait_bounded(done, 0, limit, &no_abort);
+    wait_bounded(done, 0, kDrainCycles, &no_abort);
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
@@ -496,6 +500,10 @@ sgemm_tf32x3_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   // bars: [0,S) full (leader), [S,2S) empty, 2S+{0,1} acc_full, 2S+{2,3} acc_empty (leader), 2S+4 done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * P_STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // stages whose copies each producer issued: [0] this CTA's (written by the
+  // leader's producer), [1] the partner's (written by the partner's producer
+  // into the leader's shared memory); read by the leader's drain
+  volatile int* issued_slot = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -554,6 +562,7 @@ sgemm_tf32x3_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       const uint32_t smem0 = smem_u32(smem);
       const int a_row = (int)(m0 + rank * P_BM), b_row = (int)(n0 + rank * P_BNH);
       bool ok = true;
+      int issued = 0;
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % P_STAGES;
         if (kb >= P_STAGES && !wait_bounded(empty0 + 8 * s, ((kb / P_STAGES) - 1) & 1, limit, abort_flag)) {
@@ -565,10 +574,17 @@ sgemm_tf32x3_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         const uint32_t dst = smem0 + s * P_STAGE_BYTES;
         tma_load_2d_pair(dst, &tmA, (kb0 + kb) * ROWF, a_row, bar);
         tma_load_2d_pair(dst + P_A_STAGE, &tmB, (kb0 + kb) * ROWF, b_row, bar);
+        ++issued;
       }
       if (!ok) {
         *abort_flag = 1;
         atomicOr(err, mk::ERRBIT_TIMEOUT);
+      }
+      if (leader) {
+        issued_slot[0] = issued;
+      } else {
+        const uint32_t remote = map_rank(smem_u32((const void*)(issued_slot + 1)), 0);
+        asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(remote), "r"(issued) : "memory");
       }
     }
   } else if (warp == 1) {
@@ -657,9 +673,28 @@ sgemm_tf32x3_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   __syncwarp();
   tc_fence_before();
   cluster_sync_all();  // every role of both CTAs has finished with the peer's barriers and TMEM
+  if (leader && warp == 0 && lane == 0) {
+    // Drain before either CTA exits: both CTAs' copies complete on the
+    // leader's full barriers (expect_tx counts both halves), so only the
+    // leader can see them land.  Every stage below the larger issued count
+    // minus P_STAGES was consumed, so only that window can be in flight.  A
+    // phase that one producer never issued gets its missing half completed
+    // here (and, if the leader never issued it, the leader's arrival), so the
+    // phase completes exactly when the copies that were issued have landed.
+    // On the normal path both counts equal nkb and every wait returns at once.
+    const int iL = issued_slot[0], iN = issued_slot[1];
+    const int hi = max(iL, iN);
+    volatile int no_abort = 0;
+    for (int kb = max(0, hi - P_STAGES); kb < hi; ++kb) {
+      const uint32_t bar = full0 + 8 * (kb % P_STAGES);
+      if (kb >= iL) mbar_expect_tx(bar, P_STAGE_BYTES);     // only the partner's half is coming
+      if (kb >= iN) mbar_complete_tx(bar, P_STAGE_BYTES);   // the partner's half never comes
+      wait_bounded(bar, (kb / P_STAGES) & 1, kDrainCycles, &no_abort);
+    }
+  }
   if (warp == 2) {
     volatile int no_abort = 0;
-    wait_bounded(done, 0, limit, &no_abort);  // every MMA writing this CTA's TMEM has completed
+    wait_bounded(done, 0, kDrainCycles, &no_abort);  // every MMA writing this CTA's TMEM has completed
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }

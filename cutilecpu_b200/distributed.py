@@ -125,5 +125,22 @@ class PeerReduce:
                                                      current_stream_handle()), "mapreduce allreduce")
         return out
 
+    def submit(self, x, out: torch.Tensor, f: str = "abs2", op: str = "add", init: float = 0.0) -> torch.Tensor:
+        """Pipelined ``__call__`` (``mk_mapreduce_f32_allreduce_async``): the
+        global result lands in ``out`` once the next ``submit``/``__call__``
+        or ``complete()`` has run on the stream; no rank waits for its peers
+        inside the step.  ``out`` must stay alive until then."""
+        from .array import current_stream_handle
+        L = self._lib.lib()
+        self._lib.check(L.mk_mapreduce_f32_allreduce_async(out.data_ptr(), x.pointer(), x.length,
+                                                           self._lib.MK_F[f], self._lib.MK_OP[op], float(init),
+                                                           current_stream_handle()), "mapreduce allreduce async")
+        return out
+
+    def complete(self) -> None:
+        """Write the last pending ``submit`` result (asynchronous)."""
+        from .array import current_stream_handle
+        self._lib.check(self._lib.lib().mk_allreduce_complete(current_stream_handle()), "allreduce complete")
+
     def close(self) -> None:
         self._lib.check(self._lib.lib().mk_peer_destroy(), "mk_peer_destroy")

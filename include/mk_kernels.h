@@ -238,6 +238,21 @@ MK_API int mk_peer_destroy(void);
 MK_API int mk_mapreduce_f32_allreduce(double* out_dev, const float* x, int64_t n,
                                       int f, int op, double init, void* stream);
 
+/* Pipelined form of mk_mapreduce_f32_allreduce for a stream of reductions
+ * (no counterpart in the single-GPU reference).  The launch reduces this
+ * rank's shard and publishes its partial to every rank, but does not wait
+ * for the other ranks: the global result of a call is written to its out_dev
+ * by the NEXT exchanging launch on this device (this function or the blocking
+ * one), which folds it at its end, or by mk_allreduce_complete(stream).  So a
+ * rank never stalls on a slower peer inside a step; only the completion waits.
+ * The result is bit-identical to the blocking form's.  Until it is completed,
+ * out_dev must stay allocated; all exchanging calls and the completion must
+ * be issued on one stream per device, in the same order on every rank.
+ * mk_allreduce_complete is a no-op when nothing is pending. */
+MK_API int mk_mapreduce_f32_allreduce_async(double* out_dev, const float* x, int64_t n,
+                                            int f, int op, double init, void* stream);
+MK_API int mk_allreduce_complete(void* stream);
+
 /* ---- memory pools -------------------------------------------------------
  * Device memory from a per-device stream-ordered pool that keeps freed memory
  * cached (allocation and free are ordered on `stream`); replaces the CUDA.jl

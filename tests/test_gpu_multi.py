@@ -38,10 +38,25 @@ def _worker(rank, world, port, results):
             f = "abs2" if op == "add" else "identity"
             init = 0.0 if op == "add" else -np.inf
             vals.append(pr(x, f, op, init).item())
+        # pipelined form: 9 calls in flight, completed at the end, mixed with
+        # a blocking call in the middle (which completes the pending one)
+        outs = [torch.full((1,), float("nan"), dtype=torch.float64, device="cuda") for _ in range(9)]
+        for it, o in enumerate(outs):
+            op = "add" if it % 3 else "max"
+            f = "abs2" if op == "add" else "identity"
+            init = 0.0 if op == "add" else -np.inf
+            if it == 4:
+                pr(x, f, op, init, out=o)
+            else:
+                pr.submit(x, o, f, op, init)
+        pr.complete()
+        pr.complete()  # nothing pending: a no-op
+        piped = [o.item() for o in outs]
         poll = mk._lib.lib().mk_error_poll(torch.cuda.current_stream().cuda_stream)
         pr.close()
         full = np.concatenate(shards)
-        results[rank] = {"vals": vals, "poll": poll, "sum": oracle.sum_sq(full), "max": float(full.max())}
+        results[rank] = {"vals": vals, "piped": piped, "poll": poll, "sum": oracle.sum_sq(full),
+                         "max": float(full.max())}
     finally:
         dist.destroy_process_group()
 
@@ -57,6 +72,12 @@ def test_fused_allreduce_two_gpus(cuda):
     for it, v in enumerate(r0["vals"]):
         if it % 2 == 0:
             assert v == pytest.approx(r0["sum"], rel=1e-5)
+        else:
+            assert v == r0["max"]
+    assert r0["piped"] == r1["piped"]
+    for it, v in enumerate(r0["piped"]):
+        if it % 3:
+            assert v == r0["vals"][0]  # bit-identical to the blocking form
         else:
             assert v == r0["max"]
 
