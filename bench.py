@@ -131,7 +131,8 @@ _WORKLOAD_TEXT = {
                 "semantics, exact", "input (1 GiB) larger than L2; no flush"),
     "findmax": ("findmax(x) (value, first 1-based index), Float32 x ~ U[-1,1), n=2^28 per GPU (scope row f1); "
                 "Julia order: NaN wins, +0 above -0, first index", "input (1 GiB) larger than L2; no flush"),
-    "vadd": ("vadd c=a+b Float32 n=2^20 per GPU (configs[0])", "L2 flushed (256 MiB read) before every launch"),
+    "vadd": ("vadd c=a+b Float32 n=2^20 per GPU (configs[0])",
+             "24 rotating a/b/c sets (302 MB, larger than L2): every step reads inputs from HBM; no flush"),
     "gather": ("gather c=a[idx] Float32 a 2^27 (replicated on every GPU), Int32 idx 2^27 per GPU uniform in "
                "[1,2^27] (configs[2])", "inputs (1.5 GiB) larger than L2; no flush"),
     "gather_ceiling": ("random 4-byte reads of a 2^27 Float32 array at hashed positions, 2^27 per GPU, no index "
@@ -159,7 +160,8 @@ IMPL_NOTES = {
     "matmul": "tcgen05 3xTF32 (TMEM accumulators, TMA-fed, CTA pairs); the split pre-pass is inside the step",
     "histogram": "per-block shared-memory bins, flushed with global atomics; N>1: one NCCL all-reduce of 4096 u32",
     "gather": "16-byte index/output streams, 8 random 4-byte loads in flight per thread",
-    "vadd": "16-byte loads/stores, grid of resident blocks",
+    "vadd": "16-byte loads/stores, grid of resident blocks, programmatic dependent launch; the K timed steps "
+            "run as one CUDA graph",
 }
 
 
@@ -415,29 +417,106 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
     class Vadd(Workload):
         name = "vadd"
         metric = "vadd HBM GB/s"
-        needs_l2_flush = True
         cfg = workloads.CONFIGS["vadd"]
+        # A 12 MiB vadd is launch-bound: the timed steps run as one CUDA graph
+        # of K launches (programmatic dependent launch between them), each
+        # step on the next of SETS input/output sets, which together exceed
+        # L2, so every step reads a and b from HBM without a flush kernel.
+        graph_steps = True
+        SETS = 24
 
         def __init__(self):
             super().__init__(rank, world)
             n = self.n = n_override or self.cfg["n"]
             self.a_host = workloads.uniform01(n, stream=10 + 100 * rank)
             self.b_host = workloads.uniform01(n, stream=11 + 100 * rank)
-            self.a, self.b = mk.MLIRArray(self.a_host), mk.MLIRArray(self.b_host)
-            self.c = mk.zeros(be, "Float32", n)
+            self.sets = [(mk.MLIRArray(self.a_host), mk.MLIRArray(self.b_host), mk.zeros(be, "Float32", n))
+                         for _ in range(self.SETS)]
+            self.a, self.b, self.c = self.sets[0]
+            self.cursor = 0
             self.units_per_step = 12.0 * n
             self.h2d_bytes, self.d2h_bytes = 8 * n, 4 * n
 
         def launch(self):
-            _lib.check(L.mk_vadd_f32(self.c.pointer(), self.a.pointer(), self.b.pointer(), self.n, stream()),
-                       "vadd")
+            a, b, c = self.sets[self.cursor % self.SETS]
+            self.cursor += 1
+            _lib.check(L.mk_vadd_f32(c.pointer(), a.pointer(), b.pointer(), self.n, stream()), "vadd")
 
         def combine(self):
             pass
 
         def check(self):
-            if not np.array_equal(mk.Array(self.c), self.a_host + self.b_host):
-                raise CheckFailed(f"vadd: rank {rank} differs from a+b")
+            want = self.a_host + self.b_host
+            for i, (_, _, c) in enumerate(self.sets[:min(self.cursor, self.SETS)]):
+                if not np.array_equal(mk.Array(c), want):
+                    raise CheckFailed(f"vadd: rank {rank} set {i} differs from a+b")
+
+        def graph_breakdown(self, K):
+            """CUDA-graph timing of K back-to-back launches over the rotating
+            sets: the vadd with programmatic dependent launch (the product
+            path), the same kernel launched plainly, and an empty kernel."""
+            st = torch.zeros(2, dtype=torch.int64, device="cuda")
+            res = {}
+            for label, fn in (
+                    ("graph_vadd_pdl", lambda a, b, c: L.mk_vadd_f32(c.pointer(), a.pointer(), b.pointer(), self.n,
+                                                                     stream())),
+                    ("graph_vadd_plain", lambda a, b, c: L.mk_probe_vadd_f32(2, c.pointer(), a.pointer(),
+                                                                             b.pointer(), self.n, None, stream())),
+                    ("graph_empty_kernel", lambda a, b, c: L.mk_probe_vadd_f32(0, c.pointer(), a.pointer(),
+                                                                               b.pointer(), self.n, st.data_ptr(),
+                                                                               stream()))):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    for i in range(K):
+                        _lib.check(fn(*self.sets[i % self.SETS]), label)
+                g.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                g.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                res[label] = {"per_launch_us": round(e0.elapsed_time(e1) * 1e3 / K, 2)}
+                del g
+            return res
+
+        def extra_roofline(self, K, kern_ms):
+            """Where a 12 MiB vadd's time goes (mk_probe_vadd_f32), launched
+            exactly like the timed loop (L2 flush, event, launch, event; no
+            synchronisation until the end): CUDA-event time and device-clock
+            span (first block start to last block end) of an empty kernel with
+            the same grid, a read-only pass over a and b, the vadd itself with
+            and without the L2 flush, and a bulk-copy (cp.async.bulk) vadd;
+            medians over K launches."""
+            flush = torch.ones(256 * 2**20 // 4, dtype=torch.float32, device="cuda")
+            scratch = mk.zeros(be, "Float32", self.n)
+            R = K + 3
+            out = {}
+            for label, mode, do_flush in (("empty_kernel", 0, True), ("empty_kernel_no_flush", 0, False),
+                                          ("read_a_b_only", 1, True), ("vadd", 2, True),
+                                          ("vadd_l2_resident", 2, False), ("vadd_bulk_copy", 3, True)):
+                st = torch.zeros((R, 2), dtype=torch.int64, device="cuda")
+                st[:, 0] = -1  # all ones: no block start seen yet
+                dst = scratch if mode == 1 else self.c
+                evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(R)]
+                torch.cuda.synchronize()
+                for i in range(R):
+                    if do_flush:
+                        flush.sum()
+                    evs[i][0].record()
+                    _lib.check(L.mk_probe_vadd_f32(mode, dst.pointer(), self.a.pointer(), self.b.pointer(), self.n,
+                                                   st[i].data_ptr(), stream()), "probe")
+                    evs[i][1].record()
+                torch.cuda.synchronize()
+                t = st.cpu().numpy().view(np.uint64)
+                ev = [evs[i][0].elapsed_time(evs[i][1]) * 1e3 for i in range(3, R)]
+                span = [float(t[i, 1] - t[i, 0]) * 1e-3 for i in range(3, R)]
+                out[label] = {"event_us": round(statistics.median(ev), 2),
+                              "device_span_us": round(statistics.median(span), 2)}
+                if mode in (2, 3) and not np.array_equal(mk.Array(self.c), self.a_host + self.b_host):
+                    raise CheckFailed(f"vadd probe mode {mode}: c differs from a+b")
+            out.update(self.graph_breakdown(K))
+            return {"breakdown": out}
 
         def e2e_setup(self):
             self.pa = torch.from_numpy(self.a_host).pin_memory()
@@ -864,13 +943,23 @@ def time_cpu(fn, budget_s: float = 10.0, max_reps: int = 20) -> tuple[float, int
 
 def run_ours(kind: str, args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch
-    import torch.distributed as dist
-
-    from cutilecpu_b200 import distributed
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     w = make_workload(kind, rank, world, args.n)
+    s = torch.cuda.current_stream()
+    if getattr(w, "graph_steps", False):
+        step_ms, kern_avg_max, clock_info = time_graph_steps(w, args, rank, dev, local_rank)
+    else:
+        step_ms, kern_avg_max, clock_info = time_eager_steps(w, args, rank, dev, local_rank)
+    return finish_line(w, kind, args, rank, world, dev, s, step_ms, kern_avg_max, clock_info)
+
+
+def time_eager_steps(w, args, rank: int, dev, local_rank: int):
+    """K steps launched one by one, each kernel bracketed by CUDA events."""
+    import torch
+
+    from cutilecpu_b200 import distributed
     # L2 flush between launches: READ a 256 MiB buffer (2x L2), so the lines
     # it leaves behind are clean and the next launch pays no write-backs
     flush = torch.ones(256 * 2**20 // 4, dtype=torch.float32, device=dev) if w.needs_l2_flush else None
@@ -928,6 +1017,54 @@ def run_ours(kind: str, args, rank: int, world: int, local_rank: int) -> dict | 
     step_ms = region_ms / K if flush is None else kern_avg
     step_ms = _dist_allreduce_max(step_ms)
     kern_avg_max = _dist_allreduce_max(kern_avg)
+    return step_ms, kern_avg_max, clock_info
+
+
+def time_graph_steps(w, args, rank: int, dev, local_rank: int):
+    """K steps captured as one CUDA graph and replayed once inside the timed
+    region (for launch-bound kernels); the per-step time is the region over
+    K, so the kernel time and the step time are the same number."""
+    import torch
+
+    from cutilecpu_b200 import distributed
+    s = torch.cuda.current_stream()
+    w.launch()  # first step, then its full check
+    torch.cuda.synchronize()
+    w.check()
+    for _ in range(args.warmup):
+        w.launch()
+    K = args.steps
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(K):
+            w.launch()
+    g.replay()  # the graph's own first replay (upload), untimed
+    torch.cuda.synchronize()
+    w.check()
+    distributed.barrier(device=dev)
+    clocks = ClockSampler(local_rank).start() if rank == 0 else None
+    torch.cuda.synchronize()
+    distributed.barrier(device=dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(s)
+    g.replay()
+    t1.record(s)
+    torch.cuda.synchronize()
+    distributed.barrier(device=dev)
+    clock_info = clocks.stop() if clocks is not None else None
+    step_ms = _dist_allreduce_max(t0.elapsed_time(t1) / K)
+    del g
+    return step_ms, step_ms, clock_info
+
+
+def finish_line(w, kind: str, args, rank: int, world: int, dev, s, step_ms: float, kern_avg_max: float,
+                clock_info) -> dict | None:
+    """e2e, CPU baseline, roofline and the JSON line of one workload."""
+    import torch
+
+    from cutilecpu_b200 import distributed
+    K = args.steps
 
     # end to end through the public API with pinned host buffers
     w.e2e_setup()

@@ -29,6 +29,7 @@ SIGNATURES = {
     "mk_init": (_int, [_int]),
     "mk_error_poll": (_int, [_vp]),
     "mk_vadd_f32": (_int, [_vp, _vp, _vp, _i64, _vp]),
+    "mk_probe_vadd_f32": (_int, [_int, _vp, _vp, _vp, _i64, _vp, _vp]),
     "mk_axpby_f32": (_int, [_vp, C.c_float, _vp, C.c_float, _vp, _i64, _vp]),
     "mk_mapreduce_f32": (_int, [_vp, _vp, _i64, _int, _int, _f64, _vp]),
     "mk_sum_sq_f32": (_int, [_vp, _vp, _i64, _vp]),

@@ -82,6 +82,19 @@ MK_API int mk_error_poll(void* stream);
  * examples/reflection_and_perf.jl:11-14) through ext/MLIRCUDAExt.jl:540-548. */
 MK_API int mk_vadd_f32(float* c, const float* a, const float* b, int64_t n, void* stream);
 
+/* Measurement probe with no counterpart in the reference: the parts of a
+ * small vadd's time (mode 0 empty kernel, 1 read a and b only, 2 the vector
+ * vadd, 3 a bulk-copy vadd through shared memory), each with the grid of
+ * mk_vadd_f32.  stamps[0] / stamps[1] receive the earliest block start and
+ * latest block end in ns of the device clock (the caller sets stamps[0] to
+ * ~0 and stamps[1] to 0 first; stamps may be NULL for modes 2 and 3, and
+ * mode 2 without stamps is the vector vadd launched without programmatic
+ * dependent launch).  Mode 1 writes one u32 per block into c;
+ * modes 2 and 3 write c = a + b.  a, b, c 16-byte aligned; mode 3 needs
+ * n <= SMs x 8192. */
+MK_API int mk_probe_vadd_f32(int mode, float* c, const float* a, const float* b, int64_t n,
+                             unsigned long long* stamps, void* stream);
+
 /* out[i] = alpha*x[i] + beta*y[i] (y may be NULL: out[i] = alpha*x[i]),
  * fp32 in Julia's order without FMA contraction, bit-exact.  Replaces
  * AK.map!(x -> a*x, dst, src) and broadcasts like 2f0 .* a, a .+ b

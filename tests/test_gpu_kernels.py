@@ -69,6 +69,38 @@ def test_vadd_sizes_and_misaligned_views(L, n, offset):
     assert (got[:o] == -1).all() and (got[o + n:] == -1).all()
 
 
+def test_vadd_chain_with_dependent_launch_in_a_graph(L):
+    # mk_vadd_f32 uses programmatic dependent launch: a kernel may start while
+    # its predecessor drains, but must not read before the predecessor's writes
+    # land.  A chain c1 = a + b, c2 = c1 + b, ... where each vadd reads the
+    # previous output, launched eagerly and as a CUDA graph, must equal the
+    # oracle's chain exactly.
+    n = (1 << 20) + 8
+    r = np.random.Generator(np.random.Philox(31))
+    a_h, b_h = r.random(n, dtype=np.float32), r.random(n, dtype=np.float32)
+    want = [a_h]
+    for _ in range(12):
+        want.append(oracle.vadd(want[-1], b_h))
+    b = dev(b_h)
+    for use_graph in (False, True):
+        bufs = [dev(a_h)] + [torch.full((n,), -1.0, device="cuda") for _ in range(12)]
+
+        def chain():
+            for k in range(12):
+                assert L.mk_vadd_f32(bufs[k + 1].data_ptr(), bufs[k].data_ptr(), b.data_ptr(), n, stream()) == 0
+
+        if use_graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                chain()
+            g.replay()
+        else:
+            chain()
+        torch.cuda.synchronize()
+        for k in range(13):
+            np.testing.assert_array_equal(host(bufs[k]), want[k])
+
+
 def test_vadd_empty_and_invalid(L):
     assert L.mk_vadd_f32(0, 0, 0, 0, stream()) == 0
     assert L.mk_vadd_f32(0, 0, 0, -1, stream()) == _lib.MK_ERR_INVALID
