@@ -295,6 +295,27 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
         def combine(self):
             pass  # the exchange is inside the kernel
 
+        def extra_roofline(self, K, kern_ms):
+            """N>1: where the fused exchange's time goes, from device-clock
+            stamps of K pipelined steps (mk_peer_trace): the streaming part
+            (kernel start to the last block's exchange), publishing the
+            partial to every rank, and folding the previous step's result
+            (which includes any wait for a late peer).  Medians per rank, then
+            the max over ranks."""
+            if self.peer is None:
+                return {}
+            log = torch.zeros(4 * K, dtype=torch.int64, device="cuda")
+            _lib.check(L.mk_peer_trace(log.data_ptr(), K), "trace")
+            for _ in range(K):
+                self.launch()
+            self.finish()
+            torch.cuda.synchronize()
+            _lib.check(L.mk_peer_trace(None, 0), "trace off")
+            t = log.cpu().numpy().view(np.uint64).reshape(K, 4).astype(np.int64)
+            parts = {"stream_us": t[:, 1] - t[:, 0], "publish_us": t[:, 2] - t[:, 1], "fold_us": t[:, 3] - t[:, 2]}
+            return {"exchange_trace": {k: round(_dist_allreduce_max(float(np.median(v)) * 1e-3), 2)
+                                       for k, v in parts.items()} | {"kernel_us": round(kern_ms * 1e3, 2)}}
+
         def finish(self):
             """Completes the last pending global result (timed: it is inside
             the region, after the last step)."""

@@ -86,6 +86,7 @@ mapreduce_kernel(const float* __restrict__ x, int64_t n, int head, double init,
                  double* __restrict__ out, const mk::PeerArgs peer, unsigned* __restrict__ err) {
   __shared__ double smem[kThreads / 32];
   __shared__ bool is_last;
+  if (blockIdx.x == 0 && threadIdx.x == 0) mk::peerdev::stamp(peer, 0);
   const int64_t tid = (int64_t)blockIdx.x * kThreads + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   double acc = neutral<OP>();
@@ -130,13 +131,20 @@ mapreduce_kernel(const float* __restrict__ x, int64_t n, int head, double init,
   if (tid < n - tail_start) fold1<F, OP>(acc, x[tail_start + tid]);
 
   double bsum = block_reduce<OP>(acc, smem);
+  __shared__ bool is_first;
   if (threadIdx.x == 0) {
     partials[blockIdx.x] = bsum;
     __threadfence();
     unsigned t = atomicAdd(ticket, 1u);
     is_last = (t == gridDim.x - 1);
+    is_first = (t == 0);
   }
   __syncthreads();
+  // Multi-GPU, pipelined: the first block to finish its share folds the
+  // previous call's global result while the others are still streaming, so
+  // the last block (which ends the kernel) only has to publish.
+  const bool fold_early = peer.world > 0 && peer.pend_epoch != 0 && gridDim.x > 1;
+  if (fold_early && is_first && threadIdx.x < 32) mk::peerdev::complete_pending(peer, err);
   if (!is_last) return;
   __threadfence();
   // Last block: fold the partials in a fixed order (strided per thread, then
@@ -145,24 +153,32 @@ mapreduce_kernel(const float* __restrict__ x, int64_t n, int head, double init,
   for (int b = threadIdx.x; b < (int)gridDim.x; b += kThreads) v = combine<OP>(v, __ldcg(partials + b));
   __syncthreads();  // smem reuse
   v = block_reduce<OP>(v, smem);
-  if (threadIdx.x == 0) {
-    *ticket = 0u;  // re-arm for the next reduction on this stream
+  if (threadIdx.x < 32) {  // warp 0 (v is valid in lane 0)
+    v = __shfl_sync(0xffffffffu, v, 0);
+    if (threadIdx.x == 0) *ticket = 0u;  // re-arm for the next reduction on this stream
     if (peer.world == 0) {
-      out[0] = combine<OP>(init, v);
+      if (threadIdx.x == 0) out[0] = combine<OP>(init, v);
     } else {
       // multi-GPU: publish this rank's partial, finish the previous pipelined
-      // call's global result (its partials have had a whole kernel to
-      // arrive), and in the blocking form wait for this call's own epoch
+      // call's global result unless the first block already did (its partials
+      // have had a whole kernel to arrive), and in the blocking form wait for
+      // this call's own epoch
+      if (threadIdx.x == 0) mk::peerdev::stamp(peer, 1);
       mk::peerdev::publish(v, peer);
-      mk::peerdev::complete_pending(peer, err);
-      if (peer.wait_own) out[0] = combine<OP>(init, mk::peerdev::fold(peer, peer.epoch, OP, err));
+      if (threadIdx.x == 0) mk::peerdev::stamp(peer, 2);
+      if (!fold_early) mk::peerdev::complete_pending(peer, err);
+      if (threadIdx.x == 0) mk::peerdev::stamp(peer, 3);
+      if (peer.wait_own) {
+        const double g = mk::peerdev::fold(peer, peer.epoch, OP, err);
+        if (threadIdx.x == 0) out[0] = combine<OP>(init, g);
+      }
     }
   }
 }
 
 // Completes the pending pipelined result of mk_mapreduce_f32_allreduce_async.
 __global__ void allreduce_complete_kernel(const mk::PeerArgs peer, unsigned* __restrict__ err) {
-  if (threadIdx.x == 0) mk::peerdev::complete_pending(peer, err);
+  if (threadIdx.x < 32) mk::peerdev::complete_pending(peer, err);
 }
 
 // The grid is persistent: never more blocks than fit on the GPU at once (the

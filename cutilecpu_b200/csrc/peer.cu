@@ -1,8 +1,8 @@
 // peer.cu — set-up of the peer mailboxes (see peer.cuh).  One process per
 // GPU: each rank creates its mailbox, the host side exchanges the CUDA IPC
 // handles (torch.distributed all_gather in the Python layer), and every rank
-// maps the others' mailboxes.  Epochs start at 1 and only grow, so flags never
-// need resetting; the slot ring of peer.cuh bounds how far ranks may drift.
+// maps the others' mailboxes.  Epochs start at 1 and only grow; the tagged
+// slot ring of peer.cuh needs no resetting and bounds how far ranks may drift.
 // The host keeps, per device, at most one pending pipelined result: the one
 // the next exchanging launch (or mk_allreduce_complete) writes.
 #include <cstring>
@@ -24,6 +24,8 @@ struct Mailbox {
   double* pend_out = nullptr;
   int pend_op = 0;
   double pend_init = 0.0;
+  unsigned long long* trace = nullptr;
+  int trace_len = 0;
 };
 
 std::mutex g_mu;
@@ -39,11 +41,9 @@ void fill_common(const Mailbox& m, PeerArgs* a) {
   a->world = m.world;
   a->rank = m.rank;
   a->limit = wait_limit_cycles();
-  for (int p = 0; p < m.world; ++p) {
-    char* base = static_cast<char*>(m.peers[p]);
-    a->slots[p] = reinterpret_cast<double*>(base);
-    a->flags[p] = reinterpret_cast<unsigned long long*>(base + kMailboxSlotsBytes);
-  }
+  a->trace = m.trace;
+  a->trace_len = m.trace_len;
+  for (int p = 0; p < m.world; ++p) a->slots[p] = static_cast<unsigned long long*>(m.peers[p]);
 }
 
 void take_pending(Mailbox& m, PeerArgs* a) {
@@ -159,5 +159,17 @@ extern "C" int mk_peer_destroy(void) {
   }
   if (m.local) cudaFree(m.local);
   m = Mailbox();
+  return MK_OK;
+}
+
+extern "C" int mk_peer_trace(unsigned long long* log_dev, int entries) {
+  MK_ENTRY_DEVICE(dev);
+  if (entries < 0 || (entries > 0 && !log_dev))
+    return mk::fail(MK_ERR_INVALID, "mk_peer_trace: need entries >= 0 and a device buffer of 4*entries u64");
+  std::lock_guard<std::mutex> lk(g_mu);
+  Mailbox& m = g_box[dev->id];
+  if (!m.local) return mk::fail(MK_ERR_INVALID, "mk_peer_trace: no mailbox (mk_peer_create first)");
+  m.trace = entries ? log_dev : nullptr;
+  m.trace_len = entries;
   return MK_OK;
 }

@@ -241,7 +241,10 @@ MK_API int mk_matmul_tiled16_f32(float* C, const float* A, const float* B,
  * writes its fp64 partial into every rank's mailbox over NVLink and folds
  * all ranks' partials in rank order (bounded wait; MK_ERR_TIMEOUT via
  * mk_error_poll if a rank never arrives): every rank gets the same result,
- * with no separate collective launch.  All ranks must call it the same number
+ * with no separate collective launch.  Each partial travels as one tagged
+ * 8-byte word (its 4 lowest mantissa bits carry the epoch), which leaves
+ * fp32-derived partials (max, min) exact and truncates an fp64 sum partial by
+ * at most 2^-48 relative.  All ranks must call it the same number
  * of times, on their own GPU.  mk_peer_destroy synchronises the device and
  * releases the mailbox. */
 MK_API int mk_peer_handle_size(void);
@@ -265,6 +268,13 @@ MK_API int mk_mapreduce_f32_allreduce(double* out_dev, const float* x, int64_t n
 MK_API int mk_mapreduce_f32_allreduce_async(double* out_dev, const float* x, int64_t n,
                                             int f, int op, double init, void* stream);
 MK_API int mk_allreduce_complete(void* stream);
+
+/* Diagnostic with no counterpart in the reference: when entries > 0, every
+ * exchanging launch on this device writes 4 device-clock stamps (ns of
+ * %globaltimer) into log_dev[4*(epoch % entries) ...]: kernel start, start of
+ * the last block's exchange, partial published, pending result folded.
+ * entries = 0 turns it off.  Needs the mailbox (mk_peer_create). */
+MK_API int mk_peer_trace(unsigned long long* log_dev, int entries);
 
 /* ---- memory pools -------------------------------------------------------
  * Device memory from a per-device stream-ordered pool that keeps freed memory
