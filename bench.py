@@ -158,7 +158,9 @@ IMPL_NOTES = {
               "every rank over NVLink peer memory and folds the previous step's global result (pipelined, "
               "no NCCL call); the last step's result is completed inside the timed region",
     "matmul": "tcgen05 3xTF32 (TMEM accumulators, TMA-fed, CTA pairs); the split pre-pass is inside the step",
-    "histogram": "per-block shared-memory bins, flushed with global atomics; N>1: one NCCL all-reduce of 4096 u32",
+    "histogram": "per-block shared-memory bins, flushed with global atomics; N>1: the same launch publishes the "
+                 "4096 counts (epoch-tagged words) to every rank over NVLink and folds the previous step's global "
+                 "counts (pipelined, no NCCL call)",
     "gather": "16-byte index/output streams, 8 random 4-byte loads in flight per thread",
     "vadd": "16-byte loads/stores, grid of resident blocks, programmatic dependent launch; the K timed steps "
             "run as one CUDA graph",
@@ -273,7 +275,7 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             self.x_host = workloads.uniform_pm1(n, stream=1 + 100 * rank)
             self.x = mk.MLIRArray(self.x_host)
             self.out = torch.empty(1, dtype=torch.float64, device="cuda")
-            self.peer = distributed.PeerReduce() if world > 1 else None
+            self.peer = distributed.shared_peer() if world > 1 else None
             self.outs = [torch.empty(1, dtype=torch.float64, device="cuda") for _ in range(2)]
             self.step_no = 0
             self.units_per_step = 4.0 * n
@@ -781,6 +783,9 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             self.keys_host = workloads.zipf_keys(n, nb, self.cfg["s"], stream=30 + 100 * rank)
             self.keys = mk.MLIRArray(self.keys_host)
             self.counts = mk.zeros(be, "UInt32", nb)
+            self.peer = distributed.shared_peer() if world > 1 else None
+            self.gouts = [torch.empty(nb, dtype=torch.int32, device="cuda") for _ in range(2)]
+            self.step_no = 0
             self.units_per_step = 4.0 * n
             self.h2d_bytes, self.d2h_bytes = 4 * n, 4 * nb
 
@@ -788,11 +793,29 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             self.counts.storage.zero_()  # bins accumulate: every step starts from zero
 
         def launch(self):
-            _lib.check(L.mk_hist_u32(self.counts.pointer(), self.nb, self.keys.pointer(), self.n, stream()),
-                       "hist")
+            if self.peer is not None:
+                # fused and pipelined: local counts, then this rank's counts
+                # published to every rank over NVLink and the previous step's
+                # global counts folded, in the same launch
+                self.step_no += 1
+                _lib.check(L.mk_hist_u32_allreduce_async(self.gouts[self.step_no % 2].data_ptr(),
+                                                         self.counts.pointer(), self.nb, self.keys.pointer(), self.n,
+                                                         stream()), "hist allreduce")
+            else:
+                _lib.check(L.mk_hist_u32(self.counts.pointer(), self.nb, self.keys.pointer(), self.n, stream()),
+                           "hist")
 
         def combine(self):
-            distributed.combine_counts(self.counts.storage)
+            pass  # N>1: the exchange is inside the kernel
+
+        def finish(self):
+            if self.peer is not None:
+                _lib.check(L.mk_hist_allreduce_complete(stream()), "hist complete")
+
+        def result(self):
+            if self.peer is None:
+                return mk.Array(self.counts)
+            return self.gouts[self.step_no % 2].cpu().numpy().view(np.uint32)
 
         def check(self):
             # every N: the combined counts equal the oracle's counts of all
@@ -800,7 +823,7 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
             import oracle
             mine = oracle.hist(self.keys_host, self.nb)[0].astype(np.int64)
             want = (_dist_sum_i64(mine) % (1 << 32)).astype(np.uint32)
-            got = mk.Array(self.counts)
+            got = self.result()
             if not np.array_equal(got, want):
                 bad = int(np.flatnonzero(got != want)[0])
                 raise CheckFailed(f"histogram: rank {rank} bin {bad + 1} has {got[bad]}, oracle {want[bad]}")
@@ -813,9 +836,12 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
         def e2e_step(self):
             mk.copyto(be, self.keys, self.pk)
             self.counts.storage.zero_()
-            self.k(self.counts, self.keys, ndrange=self.n)
-            distributed.combine_counts(self.counts.storage)
-            self.pc.copy_(self.counts.storage, non_blocking=True)
+            if self.peer is not None:
+                self.peer.histogram(self.counts, self.keys, self.gouts[0])
+                self.pc.copy_(self.gouts[0], non_blocking=True)
+            else:
+                self.k(self.counts, self.keys, ndrange=self.n)
+                self.pc.copy_(self.counts.storage, non_blocking=True)
             torch.cuda.current_stream().synchronize()
 
         def cpu_sample(self, threads):

@@ -52,6 +52,9 @@ SIGNATURES = {
     "mk_mapreduce_f32_allreduce_async": (_int, [_vp, _vp, _i64, _int, _int, _f64, _vp]),
     "mk_allreduce_complete": (_int, [_vp]),
     "mk_peer_trace": (_int, [_vp, _int]),
+    "mk_hist_u32_allreduce": (_int, [_vp, _vp, _i32, _vp, _i64, _vp]),
+    "mk_hist_u32_allreduce_async": (_int, [_vp, _vp, _i32, _vp, _i64, _vp]),
+    "mk_hist_allreduce_complete": (_int, [_vp]),
     "mk_pool_alloc_device": (_int, [C.POINTER(C.c_void_p), C.c_size_t, _vp]),
     "mk_pool_free_device": (_int, [_vp, _vp]),
     "mk_host_alloc_aligned": (_int, [C.POINTER(C.c_void_p), C.c_size_t, C.c_size_t]),

@@ -20,7 +20,14 @@
 //     1f0 one at a time would also be exact).
 // Bins that do not fit in shared memory use per-key global atomics.
 // Keys outside [1, nbins] are skipped and raise ERRBIT_HIST_KEY.
+//
+// Multi-GPU (mk_hist_u32_allreduce[_async]): the same kernel ends with the
+// exchange of the rank's counts over NVLink peer memory, in place of an NCCL
+// all-reduce launch: the last block to finish (atomic ticket) writes every
+// count, tagged with the epoch, into every rank's mailbox, and a pending
+// pipelined result is folded by the first block to finish (see peer.cuh).
 #include "mk_common.cuh"
+#include "peer.cuh"
 
 namespace {
 
@@ -56,10 +63,72 @@ __device__ __forceinline__ void flush_add(void* bins, uint32_t b, unsigned cnt) 
   else atomicAdd(static_cast<float*>(bins) + b, (float)cnt);
 }
 
-template <typename K, int BT>
-__global__ void __launch_bounds__(kThreads)
+// ---- exchange of u32 counts through the mailbox's histogram region --------
+
+__device__ __forceinline__ unsigned long long* hist_region(unsigned long long* mailbox) {
+  return reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(mailbox) + mk::kHistRegionOffset);
+}
+
+// Whole block: write this rank's counts of `peer.epoch` into every rank's
+// mailbox, one tagged 8-byte word per bin and peer, no fence.
+__device__ void hist_publish(const mk::PeerArgs& peer, const unsigned* counts, uint32_t nbins) {
+  const unsigned long long tag = (peer.epoch & 0xffffffffull) << 32;
+  const size_t row = ((size_t)(peer.epoch % mk::kMailboxRing) * MK_MAX_PEERS + peer.rank) * mk::kHistMaxBins;
+  for (uint32_t b = threadIdx.x; b < nbins; b += blockDim.x) {
+    const unsigned long long w = tag | __ldcg(counts + b);
+    for (int p = 0; p < peer.world; ++p)
+      asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(hist_region(peer.slots[p]) + row + b), "l"(w)
+                   : "memory");
+  }
+}
+
+// Whole block: out[b] = sum over ranks (u32, wrapping) of rank q's count of
+// `epoch`, waiting (bounded) for each word's tag.  A rank that never arrives
+// is left out and sets ERRBIT_TIMEOUT.
+__device__ void hist_fold(const mk::PeerArgs& peer, unsigned long long epoch, unsigned* out, uint32_t nbins,
+                          unsigned* err) {
+  const unsigned want = (unsigned)(epoch & 0xffffffffull);
+  const unsigned long long* mine =
+      hist_region(peer.slots[peer.rank]) + (size_t)(epoch % mk::kMailboxRing) * MK_MAX_PEERS * mk::kHistMaxBins;
+  const long long t0 = clock64();
+  bool late = false;
+  for (uint32_t b = threadIdx.x; b < nbins; b += blockDim.x) {
+    unsigned long long w[MK_MAX_PEERS];
+#pragma unroll
+    for (int q = 0; q < MK_MAX_PEERS; ++q)
+      if (q < peer.world)
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w[q]) : "l"(mine + (size_t)q * mk::kHistMaxBins + b)
+                     : "memory");
+    unsigned sum = 0u;
+#pragma unroll
+    for (int q = 0; q < MK_MAX_PEERS; ++q) {
+      if (q >= peer.world) break;
+      while ((unsigned)(w[q] >> 32) != want) {
+        if ((unsigned long long)(clock64() - t0) > peer.limit) break;
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w[q]) : "l"(mine + (size_t)q * mk::kHistMaxBins + b)
+                     : "memory");
+      }
+      if ((unsigned)(w[q] >> 32) == want) sum += (unsigned)w[q];
+      else late = true;
+    }
+    out[b] = sum;
+  }
+  if (late) atomicOr(err, mk::ERRBIT_TIMEOUT);
+}
+
+// Finishes the pending pipelined histogram result (one block).
+__global__ void __launch_bounds__(kThreads) hist_complete_kernel(const mk::PeerArgs peer, unsigned* __restrict__ err) {
+  hist_fold(peer, peer.pend_epoch, static_cast<unsigned*>(peer.pend_out), (uint32_t)peer.pend_op, err);
+}
+
+// Int32 keys: two 1024-thread blocks per SM (32 registers a thread); the
+// exchange code of the EXCH form would otherwise raise the count and halve
+// the residency.  Int64 keys need more registers and are left unconstrained.
+template <typename K, int BT, bool EXCH = false>
+__global__ void __launch_bounds__(kThreads, sizeof(K) == 4 ? kBlocksPerSM : 1)
 hist_smem(void* __restrict__ bins, uint32_t nbins, const K* __restrict__ keys, int64_t n, int head,
-          unsigned* __restrict__ err) {
+          unsigned* __restrict__ err, const mk::PeerArgs peer = mk::PeerArgs(), unsigned* __restrict__ ticket = nullptr,
+          unsigned* __restrict__ global_out = nullptr) {
   using KV = KeyVec<K>;
   using V = typename KV::V;
   extern __shared__ unsigned sh[];
@@ -94,6 +163,25 @@ hist_smem(void* __restrict__ bins, uint32_t nbins, const K* __restrict__ keys, i
   for (uint32_t b = threadIdx.x; b < nbins; b += kThreads)
     if (sh[b]) flush_add<BT>(bins, b, sh[b]);
   if (bad) atomicOr(err, mk::ERRBIT_HIST_KEY);
+  if (EXCH) {
+    // every block's flush is complete before its ticket is taken
+    __threadfence();
+    __syncthreads();
+    __shared__ unsigned tk;
+    if (threadIdx.x == 0) tk = atomicAdd(ticket, 1u);
+    __syncthreads();
+    const bool fold_early = peer.pend_epoch != 0 && gridDim.x > 1;
+    if (fold_early && tk == 0)
+      hist_fold(peer, peer.pend_epoch, static_cast<unsigned*>(peer.pend_out), (uint32_t)peer.pend_op, err);
+    if (tk == gridDim.x - 1) {
+      __threadfence();
+      if (threadIdx.x == 0) *ticket = 0u;  // re-arm for the next launch on this stream
+      hist_publish(peer, static_cast<const unsigned*>(bins), nbins);
+      if (!fold_early && peer.pend_epoch != 0)
+        hist_fold(peer, peer.pend_epoch, static_cast<unsigned*>(peer.pend_out), (uint32_t)peer.pend_op, err);
+      if (peer.wait_own) hist_fold(peer, peer.epoch, global_out, nbins, err);
+    }
+  }
 }
 
 template <typename K, int BT>
@@ -165,4 +253,62 @@ extern "C" int mk_hist(void* bins, int bin_type, int32_t nbins, const void* keys
 
 extern "C" int mk_hist_u32(uint32_t* counts, int32_t nbins, const int32_t* keys1, int64_t n, void* stream) {
   return mk_hist(counts, MK_BIN_U32, nbins, keys1, MK_KEY_I32, n, stream);
+}
+
+namespace {
+
+int hist_allreduce(bool blocking, uint32_t* global_out, uint32_t* counts, int32_t nbins, const int32_t* keys1,
+                   int64_t n, void* stream) {
+  MK_ENTRY_DEVICE(dev);
+  const char* who = blocking ? "mk_hist_u32_allreduce" : "mk_hist_u32_allreduce_async";
+  // argument errors before an epoch is taken, so a rejected call leaves the
+  // ranks' epoch counters in step
+  if (n < 0) return mk::fail(MK_ERR_INVALID, std::string(who) + ": n must be >= 0");
+  if (nbins < 1 || nbins > mk::kHistMaxBins)
+    return mk::fail(MK_ERR_INVALID, std::string(who) + ": need 1 <= nbins <= " + std::to_string(mk::kHistMaxBins));
+  if (!global_out || !counts || (n > 0 && !keys1)) return mk::fail(MK_ERR_INVALID, std::string(who) + ": null pointer");
+  if ((reinterpret_cast<uintptr_t>(keys1) & 3u) != 0 || (reinterpret_cast<uintptr_t>(counts) & 3u) != 0)
+    return mk::fail(MK_ERR_INVALID, std::string(who) + ": misaligned keys or counts");
+  const int64_t smem = (int64_t)nbins * 4;
+  if (smem > dev->max_smem_optin / kBlocksPerSM - 1024)
+    return mk::fail(MK_ERR_INVALID, std::string(who) + ": too many bins for the shared-memory kernel");
+  cudaStream_t s = mk::as_stream(stream);
+  mk::ReduceScratch rs;
+  int rc = mk::reduce_scratch(dev, s, &rs);
+  if (rc != MK_OK) return rc;
+  rc = mk::allow_dynamic_smem(reinterpret_cast<const void*>(hist_smem<int32_t, MK_BIN_U32, true>), (size_t)smem);
+  if (rc != MK_OK) return rc;
+  mk::PeerArgs peer;
+  rc = mk::peer_args_next(dev, mk::CH_HIST, &peer, blocking, global_out, nbins, 0.0);
+  if (rc != MK_OK) return rc;
+  int64_t head = n > 0 ? (int64_t)(((16u - (reinterpret_cast<uintptr_t>(keys1) & 15u)) & 15u) / 4u) : 0;
+  if (head > n) head = n;
+  int64_t blocks = mk::cdiv(n, (int64_t)kThreads * 16);
+  if (blocks > (int64_t)dev->sms * kBlocksPerSM) blocks = (int64_t)dev->sms * kBlocksPerSM;
+  if (blocks < 1) blocks = 1;
+  hist_smem<int32_t, MK_BIN_U32, true><<<(unsigned)blocks, kThreads, (size_t)smem, s>>>(
+      counts, (uint32_t)nbins, keys1, n, (int)head, dev->err_word, peer, rs.ticket, global_out);
+  return mk::check_launch(who);
+}
+
+}  // namespace
+
+extern "C" int mk_hist_u32_allreduce(uint32_t* global_out, uint32_t* counts, int32_t nbins, const int32_t* keys1,
+                                     int64_t n, void* stream) {
+  return hist_allreduce(true, global_out, counts, nbins, keys1, n, stream);
+}
+
+extern "C" int mk_hist_u32_allreduce_async(uint32_t* global_out, uint32_t* counts, int32_t nbins,
+                                           const int32_t* keys1, int64_t n, void* stream) {
+  return hist_allreduce(false, global_out, counts, nbins, keys1, n, stream);
+}
+
+extern "C" int mk_hist_allreduce_complete(void* stream) {
+  MK_ENTRY_DEVICE(dev);
+  mk::PeerArgs peer;
+  bool pending = false;
+  int rc = mk::peer_args_complete(dev, mk::CH_HIST, &peer, &pending);
+  if (rc != MK_OK || !pending) return rc;
+  hist_complete_kernel<<<1, kThreads, 0, mk::as_stream(stream)>>>(peer, dev->err_word);
+  return mk::check_launch("mk_hist_allreduce_complete: launch");
 }

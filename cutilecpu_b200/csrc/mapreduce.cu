@@ -279,7 +279,7 @@ int allreduce_entry(bool blocking, double* out_dev, const float* x, int64_t n, i
   if (n > 0 && (reinterpret_cast<uintptr_t>(x) & 3u) != 0)
     return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: x must be 4-byte aligned");
   mk::PeerArgs peer;
-  int rc = mk::peer_args_next(dev, &peer, blocking, out_dev, op, init);
+  int rc = mk::peer_args_next(dev, mk::CH_REDUCE, &peer, blocking, out_dev, op, init);
   if (rc != MK_OK) return rc;
   return mapreduce_impl(dev, out_dev, x, n, f, op, init, stream, peer);
 }
@@ -300,7 +300,7 @@ extern "C" int mk_allreduce_complete(void* stream) {
   MK_ENTRY_DEVICE(dev);
   mk::PeerArgs peer;
   bool pending = false;
-  int rc = mk::peer_args_complete(dev, &peer, &pending);
+  int rc = mk::peer_args_complete(dev, mk::CH_REDUCE, &peer, &pending);
   if (rc != MK_OK || !pending) return rc;
   allreduce_complete_kernel<<<1, 32, 0, mk::as_stream(stream)>>>(peer, dev->err_word);
   return mk::check_launch("mk_allreduce_complete: launch");

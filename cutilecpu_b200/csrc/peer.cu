@@ -17,13 +17,15 @@ struct Mailbox {
   void* local = nullptr;
   void* peers[MK_MAX_PEERS] = {};
   bool opened[MK_MAX_PEERS] = {};
-  unsigned long long epoch = 0;
   bool connected = false;
-  // pending pipelined result
-  unsigned long long pend_epoch = 0;
-  double* pend_out = nullptr;
-  int pend_op = 0;
-  double pend_init = 0.0;
+  struct Channel {
+    unsigned long long epoch = 0;
+    // pending pipelined result
+    unsigned long long pend_epoch = 0;
+    void* pend_out = nullptr;
+    int pend_op = 0;
+    double pend_init = 0.0;
+  } ch[mk::CH_COUNT];
   unsigned long long* trace = nullptr;
   int trace_len = 0;
 };
@@ -46,46 +48,48 @@ void fill_common(const Mailbox& m, PeerArgs* a) {
   for (int p = 0; p < m.world; ++p) a->slots[p] = static_cast<unsigned long long*>(m.peers[p]);
 }
 
-void take_pending(Mailbox& m, PeerArgs* a) {
-  a->pend_epoch = m.pend_epoch;
-  a->pend_out = m.pend_out;
-  a->pend_op = m.pend_op;
-  a->pend_init = m.pend_init;
-  m.pend_epoch = 0;
-  m.pend_out = nullptr;
+void take_pending(Mailbox::Channel& c, PeerArgs* a) {
+  a->pend_epoch = c.pend_epoch;
+  a->pend_out = c.pend_out;
+  a->pend_op = c.pend_op;
+  a->pend_init = c.pend_init;
+  c.pend_epoch = 0;
+  c.pend_out = nullptr;
 }
 
 }  // namespace
 
-int peer_args_next(Device* dev, PeerArgs* out, bool blocking, double* res, int op, double init) {
+int peer_args_next(Device* dev, int ch, PeerArgs* out, bool blocking, void* res, int op, double init) {
   std::lock_guard<std::mutex> lk(g_mu);
   Mailbox& m = g_box[dev->id];
   if (!m.connected) return fail(MK_ERR_INVALID, "peer mailbox of this device is not connected (mk_peer_connect)");
+  Mailbox::Channel& c = m.ch[ch];
   PeerArgs a;
   fill_common(m, &a);
-  a.epoch = ++m.epoch;
+  a.epoch = ++c.epoch;
   a.wait_own = blocking ? 1 : 0;
-  take_pending(m, &a);
+  take_pending(c, &a);
   if (!blocking) {
-    m.pend_epoch = a.epoch;
-    m.pend_out = res;
-    m.pend_op = op;
-    m.pend_init = init;
+    c.pend_epoch = a.epoch;
+    c.pend_out = res;
+    c.pend_op = op;
+    c.pend_init = init;
   }
   *out = a;
   return MK_OK;
 }
 
-int peer_args_complete(Device* dev, PeerArgs* out, bool* has_pending) {
+int peer_args_complete(Device* dev, int ch, PeerArgs* out, bool* has_pending) {
   std::lock_guard<std::mutex> lk(g_mu);
   Mailbox& m = g_box[dev->id];
   *has_pending = false;
   if (!m.connected) return fail(MK_ERR_INVALID, "peer mailbox of this device is not connected (mk_peer_connect)");
-  if (m.pend_epoch == 0) return MK_OK;
+  Mailbox::Channel& c = m.ch[ch];
+  if (c.pend_epoch == 0) return MK_OK;
   PeerArgs a;
   fill_common(m, &a);
   a.epoch = 0;
-  take_pending(m, &a);
+  take_pending(c, &a);
   *has_pending = true;
   *out = a;
   return MK_OK;
@@ -115,7 +119,7 @@ extern "C" int mk_peer_create(int world, int rank, void* handle_out) {
   std::memcpy(handle_out, &h, sizeof(h));
   m.world = world;
   m.rank = rank;
-  m.epoch = 0;
+  for (auto& c : m.ch) c = Mailbox::Channel();
   m.connected = false;
   return MK_OK;
 }

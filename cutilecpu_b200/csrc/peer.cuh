@@ -47,8 +47,8 @@ struct PeerArgs {
   int wait_own = 0;              // blocking form: also fold this call's epoch
   // an earlier pipelined call whose global result this launch writes
   unsigned long long pend_epoch = 0;  // 0: none
-  double* pend_out = nullptr;
-  int pend_op = 0;
+  void* pend_out = nullptr;           // double* (reduction) or uint32_t* (histogram)
+  int pend_op = 0;                    // reduction: operator; histogram: number of bins
   double pend_init = 0.0;
   unsigned long long* slots[MK_MAX_PEERS] = {};   // peer p's slot array
   // optional device-clock trace (mk_peer_trace): 4 u64 per epoch, ring of
@@ -59,17 +59,28 @@ struct PeerArgs {
 };
 
 constexpr size_t kMailboxSlotsBytes = (size_t)kMailboxRing * MK_MAX_PEERS * sizeof(unsigned long long);
-constexpr size_t kMailboxBytes = 4096;
+
+// Histogram region of the mailbox, after the reduction slots: u64 words
+// hist[kMailboxRing][MK_MAX_PEERS][kHistMaxBins], word = (epoch << 32) | count.
+// The full 32-bit epoch is the tag, so the word is again its own flag.
+constexpr int kHistMaxBins = 16384;
+constexpr size_t kHistRegionOffset = 4096;
+constexpr size_t kMailboxBytes =
+    kHistRegionOffset + (size_t)kMailboxRing * MK_MAX_PEERS * kHistMaxBins * sizeof(unsigned long long);
+
+// Independent streams of exchanging calls, each with its own epochs and
+// pending result.
+enum : int { CH_REDUCE = 0, CH_HIST = 1, CH_COUNT = 2 };
 
 // Arguments of the next exchanging call on the current device: a new epoch,
 // plus the pending pipelined result (if any), which this launch completes.
 // blocking=false makes this call's result the new pending one (written to
 // `out` with `op`/`init` by the next exchanging launch).  Fails when the
 // mailbox of this device is not connected.
-int peer_args_next(Device* dev, PeerArgs* out, bool blocking, double* res, int op, double init);
+int peer_args_next(Device* dev, int ch, PeerArgs* out, bool blocking, void* res, int op, double init);
 // Arguments that complete the pending pipelined result without publishing;
 // *has_pending = false when there is none.
-int peer_args_complete(Device* dev, PeerArgs* out, bool* has_pending);
+int peer_args_complete(Device* dev, int ch, PeerArgs* out, bool* has_pending);
 
 namespace peerdev {
 
@@ -165,7 +176,7 @@ __device__ __forceinline__ double fold(const PeerArgs& peer, unsigned long long 
 __device__ __forceinline__ void complete_pending(const PeerArgs& peer, unsigned* err) {
   if (peer.pend_epoch == 0) return;
   const double g = fold(peer, peer.pend_epoch, peer.pend_op, err);
-  if ((threadIdx.x & 31) == 0) peer.pend_out[0] = combine_rt(peer.pend_op, peer.pend_init, g);
+  if ((threadIdx.x & 31) == 0) static_cast<double*>(peer.pend_out)[0] = combine_rt(peer.pend_op, peer.pend_init, g);
 }
 
 }  // namespace peerdev

@@ -9,8 +9,9 @@ path:
   contiguous ranges ``[r*n/W, (r+1)*n/W)`` (``shard_range``); vadd and gather
   need no exchange;
 * mapreduce combines one fp64 partial per rank and histogram one u32 count
-  vector per rank with a single all-reduce (``combine_partial`` /
-  ``combine_counts``);
+  vector per rank: inside the kernel over NVLink peer memory (``PeerReduce``,
+  the product path), or with a single NCCL all-reduce (``combine_partial`` /
+  ``combine_counts``, kept for callers without the peer mailbox);
 * the matmul shards row blocks of A (``row_block``); B is replicated.
 
 Each function takes the process group explicitly (``None`` = the default
@@ -142,5 +143,37 @@ class PeerReduce:
         from .array import current_stream_handle
         self._lib.check(self._lib.lib().mk_allreduce_complete(current_stream_handle()), "allreduce complete")
 
+    def histogram(self, counts, keys, out: torch.Tensor, nbins: int | None = None, pipelined: bool = False):
+        """Fused multi-GPU histogram (``mk_hist_u32_allreduce[_async]``):
+        accumulate this rank's 1-based Int32 ``keys`` into its UInt32
+        ``counts`` and write the sum of every rank's counts into ``out`` (a
+        separate int32/uint32 device tensor of ``nbins`` elements), all in one
+        launch.  ``pipelined=True`` defers ``out`` to the next exchanging
+        histogram call or ``hist_complete()``."""
+        from .array import current_stream_handle
+        L = self._lib.lib()
+        nb = counts.length if nbins is None else nbins
+        fn = L.mk_hist_u32_allreduce_async if pipelined else L.mk_hist_u32_allreduce
+        self._lib.check(fn(out.data_ptr(), counts.pointer(), nb, keys.pointer(), keys.length,
+                           current_stream_handle()), "histogram allreduce")
+        return out
+
+    def hist_complete(self) -> None:
+        """Write the last pending pipelined histogram result (asynchronous)."""
+        from .array import current_stream_handle
+        self._lib.check(self._lib.lib().mk_hist_allreduce_complete(current_stream_handle()), "hist complete")
+
     def close(self) -> None:
         self._lib.check(self._lib.lib().mk_peer_destroy(), "mk_peer_destroy")
+
+
+_shared_peer: PeerReduce | None = None
+
+
+def shared_peer(group=None) -> PeerReduce:
+    """The process's one peer mailbox (a device holds one at a time): created
+    collectively on first use, then reused by every fused multi-GPU call."""
+    global _shared_peer
+    if _shared_peer is None:
+        _shared_peer = PeerReduce(group)
+    return _shared_peer

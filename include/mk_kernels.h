@@ -269,6 +269,24 @@ MK_API int mk_mapreduce_f32_allreduce_async(double* out_dev, const float* x, int
                                             int f, int op, double init, void* stream);
 MK_API int mk_allreduce_complete(void* stream);
 
+/* Fused multi-GPU histogram (no counterpart in the single-GPU reference):
+ * mk_hist_u32 into this rank's `counts`, then, in the same launch, the
+ * exchange that an NCCL all-reduce of the counts would do: global_out[b] =
+ * sum over ranks of counts[b] (u32, wrapping), on every rank.  The last block
+ * writes each count, tagged with the epoch, into every rank's mailbox over
+ * NVLink.  The blocking form waits (bounded; MK_ERR_TIMEOUT via mk_error_poll
+ * if a rank never arrives) and writes global_out before the launch ends.  The
+ * _async form does not wait: its global_out is written by the next histogram
+ * exchange on this device or by mk_hist_allreduce_complete(stream), with the
+ * same rules as mk_mapreduce_f32_allreduce_async.  1 <= nbins <= 16384;
+ * Int32 keys, UInt32 counts; counts and global_out are
+ * distinct buffers. */
+MK_API int mk_hist_u32_allreduce(uint32_t* global_out, uint32_t* counts, int32_t nbins,
+                                 const int32_t* keys1, int64_t n, void* stream);
+MK_API int mk_hist_u32_allreduce_async(uint32_t* global_out, uint32_t* counts, int32_t nbins,
+                                       const int32_t* keys1, int64_t n, void* stream);
+MK_API int mk_hist_allreduce_complete(void* stream);
+
 /* Diagnostic with no counterpart in the reference: when entries > 0, every
  * exchanging launch on this device writes 4 device-clock stamps (ns of
  * %globaltimer) into log_dev[4*(epoch % entries) ...]: kernel start, start of

@@ -61,6 +61,48 @@ def _worker(rank, world, port, results):
         dist.destroy_process_group()
 
 
+def _hist_worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import cutilecpu_b200 as mk
+    import oracle
+    from cutilecpu_b200 import distributed, workloads
+    try:
+        be = mk.MLIRCUDABackend()
+        nb = 4096
+        keys_h = [workloads.zipf_keys((1 << 22) + 5 * r, nb, 1.1, stream=30 + 100 * r) for r in range(world)]
+        keys = mk.MLIRArray(keys_h[rank])
+        pr = distributed.PeerReduce()
+        got = []
+        # blocking, then 5 pipelined steps (counts re-zeroed each step), a
+        # blocking step in the middle completing the pending one, then complete
+        outs = [torch.full((nb,), -1, dtype=torch.int32, device="cuda") for _ in range(7)]
+        for it, o in enumerate(outs):
+            counts = mk.zeros(be, "UInt32", nb)
+            pr.histogram(counts, keys, o, pipelined=it not in (0, 3))
+        pr.hist_complete()
+        pr.hist_complete()  # nothing pending: a no-op
+        got = [o.cpu().numpy().view(np.uint32) for o in outs]
+        poll = mk._lib.lib().mk_error_poll(torch.cuda.current_stream().cuda_stream)
+        pr.close()
+        want = sum(oracle.hist(k, nb)[0].astype(np.int64) for k in keys_h).astype(np.uint32)
+        results[rank] = {"ok": all(np.array_equal(g, want) for g in got), "poll": poll}
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_fused_histogram_two_gpus(cuda):
+    mgr = mp.Manager()
+    results = mgr.dict()
+    mp.spawn(_hist_worker, args=(2, _port(), results), nprocs=2, join=True)
+    for r in (0, 1):
+        assert results[r]["poll"] == 0
+        assert results[r]["ok"]
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_fused_allreduce_two_gpus(cuda):
     mgr = mp.Manager()
