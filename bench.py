@@ -1005,9 +1005,20 @@ def run_ours(kind: str, args, rank: int, world: int, local_rank: int) -> dict | 
 def hide_host_latency(us: float = 200.0) -> None:
     """Queue a ~200 us device spin before the start event, so that the GPU is
     still busy while the host enqueues the timed work: the region then holds
-    device time only, not the host's launch latency after an idle GPU."""
+    device time only, not the host's launch latency after an idle GPU.  With
+    N>1 a device-side barrier follows the spin (a blocking fused exchange of
+    zero elements through the peer mailbox), so every rank's region starts
+    when all GPUs are there, not at each host's own moment after the host
+    barrier."""
     import torch
+    import torch.distributed as dist
     torch.cuda._sleep(int(us * 1e-6 * 1.965e9))
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        from cutilecpu_b200 import _lib, distributed
+        peer = distributed.shared_peer()
+        out = torch.empty(1, dtype=torch.float64, device="cuda")
+        _lib.check(_lib.lib().mk_mapreduce_f32_allreduce(out.data_ptr(), None, 0, 0, 0, 0.0,
+                                                          torch.cuda.current_stream().cuda_stream), "device barrier")
 
 
 def time_eager_steps(w, args, rank: int, dev, local_rank: int):
