@@ -234,6 +234,18 @@ def dev_sms() -> int:
     return torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
 
 
+def _dist_gather_f64(x: float) -> list[float]:
+    """Every rank's value, in rank order (a one-element list at N=1)."""
+    import torch
+    import torch.distributed as dist
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        out = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+        dist.all_gather(out, t)
+        return [o.item() for o in out]
+    return [x]
+
+
 def _dist_sum_f64(x: float) -> float:
     import torch
     import torch.distributed as dist
@@ -1012,11 +1024,13 @@ def hide_host_latency(us: float = 200.0) -> None:
     barrier."""
     import torch
     import torch.distributed as dist
-    torch.cuda._sleep(int(us * 1e-6 * 1.965e9))
-    if dist.is_initialized() and dist.get_world_size() > 1:
+    multi = dist.is_initialized() and dist.get_world_size() > 1
+    if multi:
         from cutilecpu_b200 import _lib, distributed
-        peer = distributed.shared_peer()
+        distributed.shared_peer()  # created at start-up; never inside the spin (its set-up synchronises)
         out = torch.empty(1, dtype=torch.float64, device="cuda")
+    torch.cuda._sleep(int(us * 1e-6 * 1.965e9))
+    if multi:
         _lib.check(_lib.lib().mk_mapreduce_f32_allreduce(out.data_ptr(), None, 0, 0, 0, 0.0,
                                                           torch.cuda.current_stream().cuda_stream), "device barrier")
 
@@ -1082,7 +1096,8 @@ def time_eager_steps(w, args, rank: int, dev, local_rank: int):
     # whole-step time: the full region, or (with an L2 flush between steps)
     # the per-step kernel + combine time without the flush writes
     step_ms = region_ms / K if flush is None else kern_avg
-    step_ms = _dist_allreduce_max(step_ms)
+    w.per_rank_ms = _dist_gather_f64(step_ms)
+    step_ms = max(w.per_rank_ms)
     kern_avg_max = _dist_allreduce_max(kern_avg)
     return step_ms, kern_avg_max, clock_info
 
@@ -1121,9 +1136,10 @@ def time_graph_steps(w, args, rank: int, dev, local_rank: int):
     torch.cuda.synchronize()
     distributed.barrier(device=dev)
     clock_info = clocks.stop() if clocks is not None else None
-    step_ms = _dist_allreduce_max(t0.elapsed_time(t1) / K)
+    per_rank = _dist_gather_f64(t0.elapsed_time(t1) / K)
     del g
-    return step_ms, step_ms, clock_info
+    w.per_rank_ms = per_rank
+    return max(per_rank), max(per_rank), clock_info
 
 
 def finish_line(w, kind: str, args, rank: int, world: int, dev, s, step_ms: float, kern_avg_max: float,
@@ -1192,6 +1208,7 @@ def finish_line(w, kind: str, args, rank: int, world: int, dev, s, step_ms: floa
         "gpu_launches": K * w.launches_per_step,
         "roofline": roof,
         "kernel_ms": round(kern_avg_max, 5),
+        "step_ms_per_rank": [round(v, 5) for v in getattr(w, "per_rank_ms", [])],
         "clocks": clock_info,
         "cpu_baseline": cpu,
     }
@@ -1350,6 +1367,10 @@ def main():
     if world > 1:
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+        from cutilecpu_b200 import distributed
+        distributed.shared_peer()  # the peer mailbox, set up once before any timing (collective)
+        hide_host_latency(1.0)  # first device barrier: allocates its stream's reduction scratch now
+        torch.cuda.synchronize()
     defaults = {"reduce": (2000, 50), "maximum": (1000, 20), "findmax": (1000, 20), "vadd": (2000, 50),
                 "gather": (200, 10), "gather_ceiling": (200, 10), "histogram": (500, 20), "matmul": (20, 3),
                 "matmul_simt": (3, 1), "scan": (500, 20), "reduce_dims": (1000, 20)}
