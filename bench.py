@@ -156,11 +156,12 @@ _WORKLOAD_TEXT = {
 IMPL_NOTES = {
     "reduce": "fused single pass, fp64 accumulation; N>1: each step's kernel publishes its fp64 partial to "
               "every rank over NVLink peer memory and folds the previous step's global result (pipelined, "
-              "no NCCL call); the last step's result is completed inside the timed region",
+              "no NCCL call); the last step's result is completed inside the timed region; the K steps run "
+              "as one CUDA graph",
     "matmul": "tcgen05 3xTF32 (TMEM accumulators, TMA-fed, CTA pairs); the split pre-pass is inside the step",
     "histogram": "per-block shared-memory bins, flushed with global atomics; N>1: the same launch publishes the "
                  "4096 counts (epoch-tagged words) to every rank over NVLink and folds the previous step's global "
-                 "counts (pipelined, no NCCL call)",
+                 "counts (pipelined, no NCCL call); the K steps (counts zeroed, histogram) run as one CUDA graph",
     "gather": "16-byte index/output streams, 8 random 4-byte loads in flight per thread",
     "vadd": "16-byte loads/stores, grid of resident blocks, programmatic dependent launch; the K timed steps "
             "run as one CUDA graph",
@@ -280,6 +281,8 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
         name = "reduce"
         metric = "mapreduce sum(x.^2) HBM GB/s"
         cfg = workloads.CONFIGS["reduce"]
+        graph_steps = True     # the K steps (and, at N>1, the completion) as one CUDA graph
+        kernel_events = True   # plus an eager pass for the kernel's own duration
 
         def __init__(self):
             super().__init__(rank, world)
@@ -788,6 +791,8 @@ def make_workload(kind: str, rank: int, world: int, n_override: int | None = Non
         metric = "histogram HBM GB/s (4 B/key)"
         cfg = workloads.CONFIGS["histogram"]
         launches_per_step = 1
+        graph_steps = True     # zero the counts + histogram, K times, as one CUDA graph
+        kernel_events = True
 
         def __init__(self):
             super().__init__(rank, world)
@@ -1104,22 +1109,49 @@ def time_eager_steps(w, args, rank: int, dev, local_rank: int):
 
 def time_graph_steps(w, args, rank: int, dev, local_rank: int):
     """K steps captured as one CUDA graph and replayed once inside the timed
-    region (for launch-bound kernels); the per-step time is the region over
-    K, so the kernel time and the step time are the same number."""
+    region, so no step pays a launch gap; the per-step time is the region over
+    K.  Workloads with `kernel_events` also get a separate eager pass of K
+    launches bracketed by CUDA events, for the kernel's own duration (the
+    roofline); otherwise the kernel time is the step time."""
     import torch
 
     from cutilecpu_b200 import distributed
     s = torch.cuda.current_stream()
-    w.launch()  # first step, then its full check
+    finish = getattr(w, "finish", lambda: None)
+
+    def step():
+        w.prepare()
+        w.launch()
+        w.combine()
+
+    step()  # first step, then its full check
+    finish()
     torch.cuda.synchronize()
     w.check()
     for _ in range(args.warmup):
-        w.launch()
+        step()
+    finish()
     K = args.steps
+    kern_avg = None
+    if getattr(w, "kernel_events", False):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+        torch.cuda.synchronize()
+        distributed.barrier(device=dev)
+        hide_host_latency()
+        for i in range(K):
+            w.prepare()
+            ev[i][0].record(s)
+            w.launch()
+            ev[i][1].record(s)
+            w.combine()
+        finish()
+        torch.cuda.synchronize()
+        kern_avg = sum(a.elapsed_time(b) for a, b in ev) / K
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         for _ in range(K):
-            w.launch()
+            step()
+        finish()
     g.replay()  # the graph's own first replay (upload), untimed
     torch.cuda.synchronize()
     w.check()
@@ -1136,10 +1168,13 @@ def time_graph_steps(w, args, rank: int, dev, local_rank: int):
     torch.cuda.synchronize()
     distributed.barrier(device=dev)
     clock_info = clocks.stop() if clocks is not None else None
+    w.check()  # the timed replay's results too
     per_rank = _dist_gather_f64(t0.elapsed_time(t1) / K)
     del g
     w.per_rank_ms = per_rank
-    return max(per_rank), max(per_rank), clock_info
+    step_ms = max(per_rank)
+    kern_max = _dist_allreduce_max(kern_avg) if kern_avg is not None else step_ms
+    return step_ms, kern_max, clock_info
 
 
 def finish_line(w, kind: str, args, rank: int, world: int, dev, s, step_ms: float, kern_avg_max: float,

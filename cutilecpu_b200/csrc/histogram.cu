@@ -69,11 +69,12 @@ __device__ __forceinline__ unsigned long long* hist_region(unsigned long long* m
   return reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(mailbox) + mk::kHistRegionOffset);
 }
 
-// Whole block: write this rank's counts of `peer.epoch` into every rank's
+// Whole block: write this rank's counts of epoch e into every rank's
 // mailbox, one tagged 8-byte word per bin and peer, no fence.
-__device__ void hist_publish(const mk::PeerArgs& peer, const unsigned* counts, uint32_t nbins) {
-  const unsigned long long tag = (peer.epoch & 0xffffffffull) << 32;
-  const size_t row = ((size_t)(peer.epoch % mk::kMailboxRing) * MK_MAX_PEERS + peer.rank) * mk::kHistMaxBins;
+__device__ void hist_publish(const mk::PeerArgs& peer, unsigned long long e, const unsigned* counts,
+                             uint32_t nbins) {
+  const unsigned long long tag = (e & 0xffffffffull) << 32;
+  const size_t row = ((size_t)(e % mk::kMailboxRing) * MK_MAX_PEERS + peer.rank) * mk::kHistMaxBins;
   for (uint32_t b = threadIdx.x; b < nbins; b += blockDim.x) {
     const unsigned long long w = tag | __ldcg(counts + b);
     for (int p = 0; p < peer.world; ++p)
@@ -116,9 +117,28 @@ __device__ void hist_fold(const mk::PeerArgs& peer, unsigned long long epoch, un
   if (late) atomicOr(err, mk::ERRBIT_TIMEOUT);
 }
 
+// Whole block: if epoch e's histogram result is pending (pipelined), fold it
+// into its output and clear the record.
+__device__ void hist_complete_pending(const mk::PeerArgs& peer, unsigned long long e, unsigned* err) {
+  if (e == 0) return;
+  mk::PendingResult& r = peer.st->pend[e & 1];
+  __shared__ unsigned long long s_re;
+  __syncthreads();
+  if (threadIdx.x == 0)
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(s_re) : "l"(&r.epoch) : "memory");
+  __syncthreads();
+  if (s_re != e) return;  // nothing pending (blocking call, or already written)
+  hist_fold(peer, e, static_cast<unsigned*>(r.out), (uint32_t)r.op, err);
+  __syncthreads();
+  if (threadIdx.x == 0) r.epoch = 0;
+}
+
 // Finishes the pending pipelined histogram result (one block).
 __global__ void __launch_bounds__(kThreads) hist_complete_kernel(const mk::PeerArgs peer, unsigned* __restrict__ err) {
-  hist_fold(peer, peer.pend_epoch, static_cast<unsigned*>(peer.pend_out), (uint32_t)peer.pend_op, err);
+  __shared__ unsigned long long s_e;
+  if (threadIdx.x == 0) s_e = mk::peerdev::read_epoch(peer);
+  __syncthreads();
+  hist_complete_pending(peer, s_e, err);
 }
 
 // Int32 keys: two 1024-thread blocks per SM (32 registers a thread); the
@@ -168,18 +188,24 @@ hist_smem(void* __restrict__ bins, uint32_t nbins, const K* __restrict__ keys, i
     __threadfence();
     __syncthreads();
     __shared__ unsigned tk;
-    if (threadIdx.x == 0) tk = atomicAdd(ticket, 1u);
+    __shared__ unsigned long long s_e;  // the channel's last published epoch E
+    if (threadIdx.x == 0) {
+      s_e = mk::peerdev::read_epoch(peer);  // before the ticket (see read_epoch)
+      __threadfence();
+      tk = atomicAdd(ticket, 1u);
+    }
     __syncthreads();
-    const bool fold_early = peer.pend_epoch != 0 && gridDim.x > 1;
-    if (fold_early && tk == 0)
-      hist_fold(peer, peer.pend_epoch, static_cast<unsigned*>(peer.pend_out), (uint32_t)peer.pend_op, err);
+    const bool fold_early = gridDim.x > 1;
+    if (fold_early && tk == 0) hist_complete_pending(peer, s_e, err);
     if (tk == gridDim.x - 1) {
       __threadfence();
       if (threadIdx.x == 0) *ticket = 0u;  // re-arm for the next launch on this stream
-      hist_publish(peer, static_cast<const unsigned*>(bins), nbins);
-      if (!fold_early && peer.pend_epoch != 0)
-        hist_fold(peer, peer.pend_epoch, static_cast<unsigned*>(peer.pend_out), (uint32_t)peer.pend_op, err);
-      if (peer.wait_own) hist_fold(peer, peer.epoch, global_out, nbins, err);
+      const unsigned long long e1 = s_e + 1;
+      hist_publish(peer, e1, static_cast<const unsigned*>(bins), nbins);
+      if (!fold_early) hist_complete_pending(peer, s_e, err);
+      if (peer.mode == mk::XMODE_BLOCKING) hist_fold(peer, e1, global_out, nbins, err);
+      __syncthreads();
+      if (threadIdx.x == 0) mk::peerdev::finish_epoch(peer, e1);
     }
   }
 }
@@ -279,7 +305,8 @@ int hist_allreduce(bool blocking, uint32_t* global_out, uint32_t* counts, int32_
   rc = mk::allow_dynamic_smem(reinterpret_cast<const void*>(hist_smem<int32_t, MK_BIN_U32, true>), (size_t)smem);
   if (rc != MK_OK) return rc;
   mk::PeerArgs peer;
-  rc = mk::peer_args_next(dev, mk::CH_HIST, &peer, blocking, global_out, nbins, 0.0);
+  rc = mk::peer_args(dev, mk::CH_HIST, blocking ? mk::XMODE_BLOCKING : mk::XMODE_PIPELINED, global_out, nbins, 0.0,
+                     &peer);
   if (rc != MK_OK) return rc;
   int64_t head = n > 0 ? (int64_t)(((16u - (reinterpret_cast<uintptr_t>(keys1) & 15u)) & 15u) / 4u) : 0;
   if (head > n) head = n;
@@ -306,9 +333,8 @@ extern "C" int mk_hist_u32_allreduce_async(uint32_t* global_out, uint32_t* count
 extern "C" int mk_hist_allreduce_complete(void* stream) {
   MK_ENTRY_DEVICE(dev);
   mk::PeerArgs peer;
-  bool pending = false;
-  int rc = mk::peer_args_complete(dev, mk::CH_HIST, &peer, &pending);
-  if (rc != MK_OK || !pending) return rc;
+  int rc = mk::peer_args(dev, mk::CH_HIST, mk::XMODE_COMPLETE, nullptr, 0, 0.0, &peer);
+  if (rc != MK_OK) return rc;
   hist_complete_kernel<<<1, kThreads, 0, mk::as_stream(stream)>>>(peer, dev->err_word);
   return mk::check_launch("mk_hist_allreduce_complete: launch");
 }

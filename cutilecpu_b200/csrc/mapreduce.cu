@@ -86,7 +86,9 @@ mapreduce_kernel(const float* __restrict__ x, int64_t n, int head, double init,
                  double* __restrict__ out, const mk::PeerArgs peer, unsigned* __restrict__ err) {
   __shared__ double smem[kThreads / 32];
   __shared__ bool is_last;
-  if (blockIdx.x == 0 && threadIdx.x == 0) mk::peerdev::stamp(peer, 0);
+  __shared__ unsigned long long s_epoch;  // multi-GPU: the channel's last published epoch E
+  if (peer.trace && blockIdx.x == 0 && threadIdx.x == 0)
+    mk::peerdev::stamp(peer, mk::peerdev::read_epoch(peer) + 1, 0);
   const int64_t tid = (int64_t)blockIdx.x * kThreads + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   double acc = neutral<OP>();
@@ -134,17 +136,18 @@ mapreduce_kernel(const float* __restrict__ x, int64_t n, int head, double init,
   __shared__ bool is_first;
   if (threadIdx.x == 0) {
     partials[blockIdx.x] = bsum;
+    if (peer.world > 0) s_epoch = mk::peerdev::read_epoch(peer);  // before the ticket (see read_epoch)
     __threadfence();
     unsigned t = atomicAdd(ticket, 1u);
     is_last = (t == gridDim.x - 1);
     is_first = (t == 0);
   }
   __syncthreads();
-  // Multi-GPU, pipelined: the first block to finish its share folds the
-  // previous call's global result while the others are still streaming, so
-  // the last block (which ends the kernel) only has to publish.
-  const bool fold_early = peer.world > 0 && peer.pend_epoch != 0 && gridDim.x > 1;
-  if (fold_early && is_first && threadIdx.x < 32) mk::peerdev::complete_pending(peer, err);
+  // Multi-GPU: the first block to finish its share finishes the previous
+  // pipelined call's global result (epoch E) while the others are still
+  // streaming, so the last block (which ends the kernel) only has to publish.
+  const bool fold_early = peer.world > 0 && gridDim.x > 1;
+  if (fold_early && is_first && threadIdx.x < 32) mk::peerdev::complete_pending(peer, s_epoch, err);
   if (!is_last) return;
   __threadfence();
   // Last block: fold the partials in a fixed order (strided per thread, then
@@ -159,26 +162,27 @@ mapreduce_kernel(const float* __restrict__ x, int64_t n, int head, double init,
     if (peer.world == 0) {
       if (threadIdx.x == 0) out[0] = combine<OP>(init, v);
     } else {
-      // multi-GPU: publish this rank's partial, finish the previous pipelined
-      // call's global result unless the first block already did (its partials
-      // have had a whole kernel to arrive), and in the blocking form wait for
-      // this call's own epoch
-      if (threadIdx.x == 0) mk::peerdev::stamp(peer, 1);
-      mk::peerdev::publish(v, peer);
-      if (threadIdx.x == 0) mk::peerdev::stamp(peer, 2);
-      if (!fold_early) mk::peerdev::complete_pending(peer, err);
-      if (threadIdx.x == 0) mk::peerdev::stamp(peer, 3);
-      if (peer.wait_own) {
-        const double g = mk::peerdev::fold(peer, peer.epoch, OP, err);
+      // multi-GPU: publish this rank's partial as epoch E+1, finish epoch E's
+      // pending result unless the first block already did (its partials have
+      // had a whole kernel to arrive), and in the blocking form wait for E+1
+      const unsigned long long e1 = s_epoch + 1;
+      if (threadIdx.x == 0) mk::peerdev::stamp(peer, e1, 1);
+      mk::peerdev::publish(v, peer, e1);
+      if (threadIdx.x == 0) mk::peerdev::stamp(peer, e1, 2);
+      if (!fold_early) mk::peerdev::complete_pending(peer, s_epoch, err);
+      if (threadIdx.x == 0) mk::peerdev::stamp(peer, e1, 3);
+      if (peer.mode == mk::XMODE_BLOCKING) {
+        const double g = mk::peerdev::fold(peer, e1, OP, err);
         if (threadIdx.x == 0) out[0] = combine<OP>(init, g);
       }
+      if (threadIdx.x == 0) mk::peerdev::finish_epoch(peer, e1);
     }
   }
 }
 
 // Completes the pending pipelined result of mk_mapreduce_f32_allreduce_async.
 __global__ void allreduce_complete_kernel(const mk::PeerArgs peer, unsigned* __restrict__ err) {
-  if (threadIdx.x < 32) mk::peerdev::complete_pending(peer, err);
+  if (threadIdx.x < 32) mk::peerdev::complete_pending(peer, mk::peerdev::read_epoch(peer), err);
 }
 
 // The grid is persistent: never more blocks than fit on the GPU at once (the
@@ -279,7 +283,8 @@ int allreduce_entry(bool blocking, double* out_dev, const float* x, int64_t n, i
   if (n > 0 && (reinterpret_cast<uintptr_t>(x) & 3u) != 0)
     return mk::fail(MK_ERR_INVALID, "mk_mapreduce_f32: x must be 4-byte aligned");
   mk::PeerArgs peer;
-  int rc = mk::peer_args_next(dev, mk::CH_REDUCE, &peer, blocking, out_dev, op, init);
+  int rc = mk::peer_args(dev, mk::CH_REDUCE, blocking ? mk::XMODE_BLOCKING : mk::XMODE_PIPELINED, out_dev, op,
+                         init, &peer);
   if (rc != MK_OK) return rc;
   return mapreduce_impl(dev, out_dev, x, n, f, op, init, stream, peer);
 }
@@ -299,9 +304,8 @@ extern "C" int mk_mapreduce_f32_allreduce_async(double* out_dev, const float* x,
 extern "C" int mk_allreduce_complete(void* stream) {
   MK_ENTRY_DEVICE(dev);
   mk::PeerArgs peer;
-  bool pending = false;
-  int rc = mk::peer_args_complete(dev, mk::CH_REDUCE, &peer, &pending);
-  if (rc != MK_OK || !pending) return rc;
+  int rc = mk::peer_args(dev, mk::CH_REDUCE, mk::XMODE_COMPLETE, nullptr, 0, 0.0, &peer);
+  if (rc != MK_OK) return rc;
   allreduce_complete_kernel<<<1, 32, 0, mk::as_stream(stream)>>>(peer, dev->err_word);
   return mk::check_launch("mk_allreduce_complete: launch");
 }

@@ -3,8 +3,8 @@
 // handles (torch.distributed all_gather in the Python layer), and every rank
 // maps the others' mailboxes.  Epochs start at 1 and only grow; the tagged
 // slot ring of peer.cuh needs no resetting and bounds how far ranks may drift.
-// The host keeps, per device, at most one pending pipelined result: the one
-// the next exchanging launch (or mk_allreduce_complete) writes.
+// The epochs and the pending pipelined results live in the device mailbox
+// (peer.cuh: ChannelState), not here.
 #include <cstring>
 #include <mutex>
 
@@ -18,14 +18,6 @@ struct Mailbox {
   void* peers[MK_MAX_PEERS] = {};
   bool opened[MK_MAX_PEERS] = {};
   bool connected = false;
-  struct Channel {
-    unsigned long long epoch = 0;
-    // pending pipelined result
-    unsigned long long pend_epoch = 0;
-    void* pend_out = nullptr;
-    int pend_op = 0;
-    double pend_init = 0.0;
-  } ch[mk::CH_COUNT];
   unsigned long long* trace = nullptr;
   int trace_len = 0;
 };
@@ -48,50 +40,20 @@ void fill_common(const Mailbox& m, PeerArgs* a) {
   for (int p = 0; p < m.world; ++p) a->slots[p] = static_cast<unsigned long long*>(m.peers[p]);
 }
 
-void take_pending(Mailbox::Channel& c, PeerArgs* a) {
-  a->pend_epoch = c.pend_epoch;
-  a->pend_out = c.pend_out;
-  a->pend_op = c.pend_op;
-  a->pend_init = c.pend_init;
-  c.pend_epoch = 0;
-  c.pend_out = nullptr;
-}
-
 }  // namespace
 
-int peer_args_next(Device* dev, int ch, PeerArgs* out, bool blocking, void* res, int op, double init) {
+int peer_args(Device* dev, int ch, int mode, void* out, int op, double init, PeerArgs* a) {
   std::lock_guard<std::mutex> lk(g_mu);
   Mailbox& m = g_box[dev->id];
   if (!m.connected) return fail(MK_ERR_INVALID, "peer mailbox of this device is not connected (mk_peer_connect)");
-  Mailbox::Channel& c = m.ch[ch];
-  PeerArgs a;
-  fill_common(m, &a);
-  a.epoch = ++c.epoch;
-  a.wait_own = blocking ? 1 : 0;
-  take_pending(c, &a);
-  if (!blocking) {
-    c.pend_epoch = a.epoch;
-    c.pend_out = res;
-    c.pend_op = op;
-    c.pend_init = init;
-  }
-  *out = a;
-  return MK_OK;
-}
-
-int peer_args_complete(Device* dev, int ch, PeerArgs* out, bool* has_pending) {
-  std::lock_guard<std::mutex> lk(g_mu);
-  Mailbox& m = g_box[dev->id];
-  *has_pending = false;
-  if (!m.connected) return fail(MK_ERR_INVALID, "peer mailbox of this device is not connected (mk_peer_connect)");
-  Mailbox::Channel& c = m.ch[ch];
-  if (c.pend_epoch == 0) return MK_OK;
-  PeerArgs a;
-  fill_common(m, &a);
-  a.epoch = 0;
-  take_pending(c, &a);
-  *has_pending = true;
-  *out = a;
+  PeerArgs p;
+  fill_common(m, &p);
+  p.mode = mode;
+  p.st = reinterpret_cast<ChannelState*>(static_cast<char*>(m.local) + kChannelStateOffset) + ch;
+  p.out = out;
+  p.op = op;
+  p.init = init;
+  *a = p;
   return MK_OK;
 }
 
@@ -119,7 +81,6 @@ extern "C" int mk_peer_create(int world, int rank, void* handle_out) {
   std::memcpy(handle_out, &h, sizeof(h));
   m.world = world;
   m.rank = rank;
-  for (auto& c : m.ch) c = Mailbox::Channel();
   m.connected = false;
   return MK_OK;
 }

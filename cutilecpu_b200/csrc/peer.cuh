@@ -39,17 +39,38 @@ namespace mk {
 constexpr int kMailboxRing = 4;
 constexpr int kTagBits = 4;
 
+// Per-channel exchange state, kept in the rank's OWN mailbox (peers never
+// read it) so that no launch depends on host-side bookkeeping: a launch reads
+// the last published epoch E from here, publishes E+1, and the pipelined
+// form records where its global result goes; the next launch (or the
+// completion kernel) finds that record here.  Launches of the exchanging entry
+// points can therefore be captured in a CUDA graph and replayed.
+struct PendingResult {
+  unsigned long long epoch;  // the epoch this record describes; cleared to 0 once written
+  void* out;                 // double* (reduction) or uint32_t* (histogram)
+  int op;                    // reduction: operator; histogram: number of bins
+  int pad;
+  double init;
+};
+struct ChannelState {
+  unsigned long long epoch;  // last epoch this rank published on the channel
+  unsigned long long pad;
+  PendingResult pend[2];     // by epoch parity: launch E+1 writes pend[(E+1)&1] while pend[E&1] is finished
+};
+
+// What a launch does with the channel.
+enum : int { XMODE_NONE = 0, XMODE_PIPELINED = 1, XMODE_BLOCKING = 2, XMODE_COMPLETE = 3 };
+
 struct PeerArgs {
   int world = 0;  // 0: no exchange (single-GPU reduction)
   int rank = 0;
-  unsigned long long epoch = 0;  // epoch this call publishes; 0: publishes nothing
+  int mode = XMODE_NONE;
   unsigned long long limit = 0;  // bounded-wait budget in SM cycles
-  int wait_own = 0;              // blocking form: also fold this call's epoch
-  // an earlier pipelined call whose global result this launch writes
-  unsigned long long pend_epoch = 0;  // 0: none
-  void* pend_out = nullptr;           // double* (reduction) or uint32_t* (histogram)
-  int pend_op = 0;                    // reduction: operator; histogram: number of bins
-  double pend_init = 0.0;
+  ChannelState* st = nullptr;    // this rank's channel state (device memory)
+  // this call's result: where it goes and how it is finished
+  void* out = nullptr;
+  int op = 0;                    // reduction: operator; histogram: number of bins
+  double init = 0.0;
   unsigned long long* slots[MK_MAX_PEERS] = {};   // peer p's slot array
   // optional device-clock trace (mk_peer_trace): 4 u64 per epoch, ring of
   // trace_len entries: [kernel start, last block's exchange start, published,
@@ -59,6 +80,7 @@ struct PeerArgs {
 };
 
 constexpr size_t kMailboxSlotsBytes = (size_t)kMailboxRing * MK_MAX_PEERS * sizeof(unsigned long long);
+constexpr size_t kChannelStateOffset = 2048;  // the local channel states, after the reduction slots
 
 // Histogram region of the mailbox, after the reduction slots: u64 words
 // hist[kMailboxRing][MK_MAX_PEERS][kHistMaxBins], word = (epoch << 32) | count.
@@ -71,16 +93,14 @@ constexpr size_t kMailboxBytes =
 // Independent streams of exchanging calls, each with its own epochs and
 // pending result.
 enum : int { CH_REDUCE = 0, CH_HIST = 1, CH_COUNT = 2 };
+static_assert(kMailboxSlotsBytes <= kChannelStateOffset, "reduction slots overlap the channel states");
+static_assert(kChannelStateOffset + CH_COUNT * sizeof(ChannelState) <= kHistRegionOffset,
+              "channel states overlap the histogram region");
 
-// Arguments of the next exchanging call on the current device: a new epoch,
-// plus the pending pipelined result (if any), which this launch completes.
-// blocking=false makes this call's result the new pending one (written to
-// `out` with `op`/`init` by the next exchanging launch).  Fails when the
-// mailbox of this device is not connected.
-int peer_args_next(Device* dev, int ch, PeerArgs* out, bool blocking, void* res, int op, double init);
-// Arguments that complete the pending pipelined result without publishing;
-// *has_pending = false when there is none.
-int peer_args_complete(Device* dev, int ch, PeerArgs* out, bool* has_pending);
+// Arguments of an exchanging launch on the current device (mode, and this
+// call's result description).  Reads no per-call host state, so the launch
+// may be captured in a graph.  Fails when the mailbox is not connected.
+int peer_args(Device* dev, int ch, int mode, void* out, int op, double init, PeerArgs* a);
 
 namespace peerdev {
 
@@ -92,9 +112,33 @@ __device__ __forceinline__ unsigned long long now_ns() {
   return t;
 }
 
-// Trace slot k (0..3) of this launch's epoch, if tracing is on.
-__device__ __forceinline__ void stamp(const PeerArgs& peer, int k) {
-  if (peer.trace && peer.epoch) peer.trace[(peer.epoch % (unsigned long long)peer.trace_len) * 4 + k] = now_ns();
+// Trace slot k (0..3) of epoch e, if tracing is on.
+__device__ __forceinline__ void stamp(const PeerArgs& peer, unsigned long long e, int k) {
+  if (peer.trace) peer.trace[(e % (unsigned long long)peer.trace_len) * 4 + k] = now_ns();
+}
+
+// The channel's last published epoch.  Read by thread 0 of every block
+// BEFORE its ticket: the increment happens only in the last block, after all
+// tickets, so every block of a launch reads the same value.
+__device__ __forceinline__ unsigned long long read_epoch(const PeerArgs& peer) {
+  unsigned long long e;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(e) : "l"(&peer.st->epoch) : "memory");
+  return e;
+}
+
+// One thread, at the end of the last block: epoch E+1 is now the channel's
+// last published epoch; in the pipelined form, record where its result goes.
+__device__ __forceinline__ void finish_epoch(const PeerArgs& peer, unsigned long long e1) {
+  if (peer.mode == XMODE_PIPELINED) {
+    PendingResult& r = peer.st->pend[e1 & 1];
+    r.out = peer.out;
+    r.op = peer.op;
+    r.init = peer.init;
+    __threadfence();
+    r.epoch = e1;
+  }
+  __threadfence();
+  peer.st->epoch = e1;
 }
 
 __device__ __forceinline__ double combine_rt(int op, double a, double b) {
@@ -126,14 +170,14 @@ __device__ __forceinline__ unsigned long long tag_word(double v, unsigned long l
 
 __device__ __forceinline__ double untag(unsigned long long w) { return __longlong_as_double((long long)(w & ~kTagMask)); }
 
-// One warp (all 32 lanes): lane p writes this rank's tagged partial of
-// `peer.epoch` into rank p's mailbox over NVLink (one relaxed 8-byte store
-// each, no fence).  `mine` must be the same on every lane.
-__device__ __forceinline__ void publish(double mine, const PeerArgs& peer) {
+// One warp (all 32 lanes): lane p writes this rank's tagged partial of epoch
+// e into rank p's mailbox over NVLink (one relaxed 8-byte store each, no
+// fence).  `mine` must be the same on every lane.
+__device__ __forceinline__ void publish(double mine, const PeerArgs& peer, unsigned long long e) {
   const int lane = threadIdx.x & 31;
   if (lane < peer.world) {
-    const unsigned long long w = tag_word(mine, peer.epoch);
-    const int slot = (int)(peer.epoch % kMailboxRing);
+    const unsigned long long w = tag_word(mine, e);
+    const int slot = (int)(e % kMailboxRing);
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(peer.slots[lane] + slot * MK_MAX_PEERS + peer.rank),
                  "l"(w)
                  : "memory");
@@ -172,11 +216,19 @@ __device__ __forceinline__ double fold(const PeerArgs& peer, unsigned long long 
   return acc;
 }
 
-// One warp: finish the pending pipelined result, if the launch carries one.
-__device__ __forceinline__ void complete_pending(const PeerArgs& peer, unsigned* err) {
-  if (peer.pend_epoch == 0) return;
-  const double g = fold(peer, peer.pend_epoch, peer.pend_op, err);
-  if ((threadIdx.x & 31) == 0) static_cast<double*>(peer.pend_out)[0] = combine_rt(peer.pend_op, peer.pend_init, g);
+// One warp: if epoch e's result is pending (pipelined), fold it and write it.
+__device__ __forceinline__ void complete_pending(const PeerArgs& peer, unsigned long long e, unsigned* err) {
+  if (e == 0) return;
+  PendingResult& r = peer.st->pend[e & 1];
+  unsigned long long re;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(re) : "l"(&r.epoch) : "memory");
+  if (re != e) return;  // nothing pending (blocking call, or already written)
+  const int op = r.op;
+  const double g = fold(peer, e, op, err);
+  if ((threadIdx.x & 31) == 0) {
+    static_cast<double*>(r.out)[0] = combine_rt(op, r.init, g);
+    r.epoch = 0;
+  }
 }
 
 }  // namespace peerdev

@@ -52,10 +52,24 @@ def _worker(rank, world, port, results):
         pr.complete()
         pr.complete()  # nothing pending: a no-op
         piped = [o.item() for o in outs]
+        # the exchange keeps its epochs and pending result in device memory, so
+        # pipelined calls captured in a CUDA graph can be replayed
+        gouts = [torch.full((1,), float("nan"), dtype=torch.float64, device="cuda") for _ in range(3)]
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for o in gouts:
+                pr.submit(x, o)
+            pr.complete()
+        graphed = []
+        for _ in range(3):
+            for o in gouts:
+                o.fill_(float("nan"))
+            g.replay()
+            graphed.append([o.item() for o in gouts])
         poll = mk._lib.lib().mk_error_poll(torch.cuda.current_stream().cuda_stream)
         pr.close()
         full = np.concatenate(shards)
-        results[rank] = {"vals": vals, "piped": piped, "poll": poll, "sum": oracle.sum_sq(full),
+        results[rank] = {"vals": vals, "piped": piped, "graphed": graphed, "poll": poll, "sum": oracle.sum_sq(full),
                          "max": float(full.max())}
     finally:
         dist.destroy_process_group()
@@ -85,6 +99,20 @@ def _hist_worker(rank, world, port, results):
         pr.hist_complete()
         pr.hist_complete()  # nothing pending: a no-op
         got = [o.cpu().numpy().view(np.uint32) for o in outs]
+        # captured in a CUDA graph (counts zeroed inside), replayed twice
+        counts = mk.zeros(be, "UInt32", nb)
+        gouts = [torch.full((nb,), -1, dtype=torch.int32, device="cuda") for _ in range(2)]
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for o in gouts:
+                counts.storage.zero_()
+                pr.histogram(counts, keys, o, pipelined=True)
+            pr.hist_complete()
+        for _ in range(2):
+            for o in gouts:
+                o.fill_(-1)
+            g.replay()
+            got += [o.cpu().numpy().view(np.uint32) for o in gouts]
         poll = mk._lib.lib().mk_error_poll(torch.cuda.current_stream().cuda_stream)
         pr.close()
         want = sum(oracle.hist(k, nb)[0].astype(np.int64) for k in keys_h).astype(np.uint32)
@@ -117,6 +145,9 @@ def test_fused_allreduce_two_gpus(cuda):
         else:
             assert v == r0["max"]
     assert r0["piped"] == r1["piped"]
+    assert r0["graphed"] == r1["graphed"]
+    for rep in r0["graphed"]:
+        assert rep == [r0["vals"][0]] * 3  # every replay, bit-identical to the eager blocking form
     for it, v in enumerate(r0["piped"]):
         if it % 3:
             assert v == r0["vals"][0]  # bit-identical to the blocking form
