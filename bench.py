@@ -1147,8 +1147,18 @@ def time_graph_steps(w, args, rank: int, dev, local_rank: int):
         finish()
         torch.cuda.synchronize()
         kern_avg = sum(a.elapsed_time(b) for a, b in ev) / K
+    # capture on a dedicated stream that has run the steps once already: the
+    # library's per-stream scratch is allocated on a stream's first use, which
+    # cannot happen during capture
+    cap = torch.cuda.Stream()
+    cap.wait_stream(s)
+    with torch.cuda.stream(cap):
+        step()
+        finish()
+    s.wait_stream(cap)
+    torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
+    with torch.cuda.graph(g, stream=cap):
         for _ in range(K):
             step()
         finish()

@@ -55,8 +55,13 @@ def _worker(rank, world, port, results):
         # the exchange keeps its epochs and pending result in device memory, so
         # pipelined calls captured in a CUDA graph can be replayed
         gouts = [torch.full((1,), float("nan"), dtype=torch.float64, device="cuda") for _ in range(3)]
+        cap = torch.cuda.Stream()  # warmed first: per-stream scratch is allocated on first use, not in capture
+        with torch.cuda.stream(cap):
+            pr.submit(x, gouts[0])
+            pr.complete()
+        torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+        with torch.cuda.graph(g, stream=cap):
             for o in gouts:
                 pr.submit(x, o)
             pr.complete()
@@ -102,8 +107,14 @@ def _hist_worker(rank, world, port, results):
         # captured in a CUDA graph (counts zeroed inside), replayed twice
         counts = mk.zeros(be, "UInt32", nb)
         gouts = [torch.full((nb,), -1, dtype=torch.int32, device="cuda") for _ in range(2)]
+        cap = torch.cuda.Stream()
+        with torch.cuda.stream(cap):
+            counts.storage.zero_()
+            pr.histogram(counts, keys, gouts[0], pipelined=True)
+            pr.hist_complete()
+        torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+        with torch.cuda.graph(g, stream=cap):
             for o in gouts:
                 counts.storage.zero_()
                 pr.histogram(counts, keys, o, pipelined=True)
