@@ -512,3 +512,45 @@ def test_findmax_surface(L):
     assert mk.extrema(a) == (float(fx.min()), float(fx.max()))
     s = mk.MLIRArray(fx - np.float32(0.5))
     assert mk.any_(mk.positive, s) and not mk.all_(mk.positive, s)
+
+
+# ------------------------------------------------------ measurement probes -----
+
+def _mix32(h: np.ndarray) -> np.ndarray:
+    h = h.astype(np.uint64)
+    h ^= h >> np.uint64(16)
+    h = (h * np.uint64(0x85EBCA6B)) & np.uint64(0xFFFFFFFF)
+    h ^= h >> np.uint64(13)
+    h = (h * np.uint64(0xC2B2AE35)) & np.uint64(0xFFFFFFFF)
+    h ^= h >> np.uint64(16)
+    return h
+
+
+@pytest.mark.parametrize("n,na", [(1000, 777), ((1 << 20) + 5, 1 << 20)])
+def test_random_read_probe_reads_the_hashed_positions(L, n, na):
+    # the XOR of all per-block words equals the XOR of a[hash(i) * na >> 32]
+    r = np.random.Generator(np.random.Philox(na))
+    a_h = r.random(na, dtype=np.float32)
+    a = dev(a_h)
+    sums = torch.zeros(torch.cuda.get_device_properties(0).multi_processor_count * 8, dtype=torch.int32,
+                       device="cuda")
+    assert L.mk_probe_random_read_f32(sums.data_ptr(), sums.numel(), a.data_ptr(), na, n, 11, stream()) == 0
+    pos = (_mix32(np.arange(n, dtype=np.uint32) ^ np.uint32(11)) * np.uint64(na)) >> np.uint64(32)
+    want = np.bitwise_xor.reduce(a_h.view(np.uint32)[pos])
+    assert np.bitwise_xor.reduce(host(sums).view(np.uint32)) == want
+    assert L.mk_probe_random_read_f32(sums.data_ptr(), 4, a.data_ptr(), na, n, 0, stream()) == _lib.MK_ERR_INVALID
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+def test_vadd_probe_modes(L, mode):
+    n = 1 << 20
+    r = np.random.Generator(np.random.Philox(mode))
+    a_h, b_h = r.random(n, dtype=np.float32), r.random(n, dtype=np.float32)
+    a, b = dev(a_h), dev(b_h)
+    c = torch.zeros(n, device="cuda")
+    st = torch.tensor([-1, 0], dtype=torch.int64, device="cuda")
+    assert L.mk_probe_vadd_f32(mode, c.data_ptr(), a.data_ptr(), b.data_ptr(), n, st.data_ptr(), stream()) == 0
+    t = host(st).view(np.uint64)
+    assert t[0] != np.uint64(0xFFFFFFFFFFFFFFFF) and t[1] >= t[0]  # both stamps written, in order
+    if mode in (2, 3):
+        np.testing.assert_array_equal(host(c), oracle.vadd(a_h, b_h))
