@@ -146,11 +146,37 @@ __global__ void __launch_bounds__(256) split_a(float* __restrict__ A2, const flo
   const int64_t m0 = (int64_t)blockIdx.x * SA_ROWS;
   const int kb0 = blockIdx.y * SA_KBS;
   const int nk = min(SA_KBS, nkb - kb0) * KB;
-  for (int e = threadIdx.x; e < SA_KBS * KB * SA_ROWS; e += 256) {
-    const int kk = e / SA_ROWS, mm = e % SA_ROWS;
-    const int64_t m = m0 + mm;
-    const int64_t k = (int64_t)kb0 * KB + kk;  // columns at or past kvalid are zero padding
-    t[kk][mm] = (kk < nk && m < M && k < kvalid) ? A[m + k * lda] : 0.0f;
+  // 16-byte loads along m (A is column-major) when A, lda and the block's
+  // rows allow them: all of the block's loads are then issued before any is
+  // used; otherwise one 4-byte load per element
+  const bool vec = ((reinterpret_cast<uintptr_t>(A) & 15u) == 0) && (lda & 3) == 0 && m0 + SA_ROWS <= M;
+  if (vec) {
+    constexpr int kV = SA_KBS * KB * SA_ROWS / 4 / 256;  // float4 per thread
+    float4 q[kV];
+#pragma unroll
+    for (int u = 0; u < kV; ++u) {
+      const int e = u * 256 + threadIdx.x;
+      const int kk = e / (SA_ROWS / 4), m4 = e % (SA_ROWS / 4);
+      const int64_t k = (int64_t)kb0 * KB + kk;  // columns at or past kvalid are zero padding
+      q[u] = (kk < nk && k < kvalid) ? __ldcs(reinterpret_cast<const float4*>(A + m0 + 4 * m4 + k * lda))
+                                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+#pragma unroll
+    for (int u = 0; u < kV; ++u) {
+      const int e = u * 256 + threadIdx.x;
+      const int kk = e / (SA_ROWS / 4), m4 = e % (SA_ROWS / 4);
+      t[kk][4 * m4] = q[u].x;
+      t[kk][4 * m4 + 1] = q[u].y;
+      t[kk][4 * m4 + 2] = q[u].z;
+      t[kk][4 * m4 + 3] = q[u].w;
+    }
+  } else {
+    for (int e = threadIdx.x; e < SA_KBS * KB * SA_ROWS; e += 256) {
+      const int kk = e / SA_ROWS, mm = e % SA_ROWS;
+      const int64_t m = m0 + mm;
+      const int64_t k = (int64_t)kb0 * KB + kk;  // columns at or past kvalid are zero padding
+      t[kk][mm] = (kk < nk && m < M && k < kvalid) ? A[m + k * lda] : 0.0f;
+    }
   }
   __syncthreads();
   const int64_t row_len = (int64_t)nkb * ROWF;
