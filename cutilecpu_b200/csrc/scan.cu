@@ -65,13 +65,13 @@ __device__ __forceinline__ unsigned long long peek(const unsigned long long* p) 
 // raised and `init` is used, so no successor waits forever.
 template <int OP>
 __device__ double look_back(ScanState st, int64_t t, double block_total, double init, unsigned long long limit,
-                            unsigned* err) {
+                            unsigned* err, bool agg_published) {
   const int lane = threadIdx.x & 31;
   double prefix;
   if (t == 0) {
     prefix = init;
   } else {
-    if (lane == 0) publish(st.word + t, pack(block_total, 0u));
+    if (lane == 0 && !agg_published) publish(st.word + t, pack(block_total, 0u));
     double acc = neutral<OP>();
     int64_t j = t - 1 - lane;  // lane i looks at tile t-1-i
     bool found = false, timed_out = false;
@@ -123,6 +123,7 @@ scan_kernel(float* out, const float* x,  // may alias: a tile reads all of its i
             ScanState st, unsigned long long limit, unsigned* __restrict__ err) {
   extern __shared__ float4 buf4[];  // kTile / 4 chunks
   __shared__ double warp_tot[kThreads / 32];
+  __shared__ double warp_agg[kThreads / 32];  // early tile aggregate, per warp
   __shared__ unsigned s_tile;
   __shared__ double s_prefix;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -144,12 +145,33 @@ scan_kernel(float* out, const float* x,  // may alias: a tile reads all of its i
       const int f = i * kThreads + tid;
       buf4[slot(f >> 3, f & 7)] = q[i];
     }
+    // the tile's aggregate straight from the registers, so that successors
+    // can use it before this tile has scanned anything (any fixed grouping:
+    // it differs from the scan's own total only in rounding)
+    float v[kPer / 4];
+#pragma unroll
+    for (int i = 0; i < kPer / 4; ++i)
+      v[i] = combine32<OP>(combine32<OP>(q[i].x, q[i].y), combine32<OP>(q[i].z, q[i].w));
+#pragma unroll
+    for (int w = 1; w < kPer / 4; w <<= 1)
+#pragma unroll
+      for (int j = 0; j + w < kPer / 4; j += 2 * w) v[j] = combine32<OP>(v[j], v[j + w]);
+    double a = (double)v[0];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = combine<OP>(a, __shfl_xor_sync(0xffffffffu, a, o));
+    if (lane == 0) warp_agg[warp] = a;
   } else {
     float* buf = reinterpret_cast<float*>(buf4);
     for (int e = tid; e < kTile; e += kThreads)
       buf[slot(e >> 5, (e >> 2) & 7) * 4 + (e & 3)] = e < cnt ? x[base + e] : neutral32<OP>();
   }
   __syncthreads();
+  if (vec && warp == 0 && t > 0) {
+    double a = lane < kThreads / 32 ? warp_agg[lane] : neutral<OP>();
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) a = combine<OP>(a, __shfl_xor_sync(0xffffffffu, a, o));
+    if (lane == 0) publish(st.word + t, pack(a, 0u));
+  }
 
   float4* row = buf4 + tid * 8;
   const int sw = tid & 7;
@@ -194,7 +216,7 @@ scan_kernel(float* out, const float* x,  // may alias: a tile reads all of its i
 
   // decoupled look-back (warp 0)
   if (warp == 0) {
-    const double prefix = look_back<OP>(st, (int64_t)t, block_total, init, limit, err);
+    const double prefix = look_back<OP>(st, (int64_t)t, block_total, init, limit, err, vec);
     if (lane == 0) s_prefix = prefix;
   }
   __syncthreads();
