@@ -13,6 +13,12 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kUnroll = 2;  // float4 per operand in flight per thread
+// Grid cap of the vector kernel: 5 blocks of 256 per SM (740 on a B200), not
+// the 8 that fill every thread slot.  With PDL the next launch's blocks become
+// resident while this one drains; at 2^20 elements in a CUDA graph a step
+// took 3.41-3.44 us at 5 per SM against 3.58-3.62 at 8, 3.47 at 4 and 3.93
+// at 2, and 2^24 / 2^26 streams stayed within 2 % of the 8-per-SM grid.
+constexpr int kVecBlocksPerSM = 5;
 
 // Device-clock stamps of a launch (probe builds only): [0] earliest block
 // start, [1] latest block end, in ns of %globaltimer.
@@ -89,11 +95,12 @@ extern "C" int mk_vadd_f32(float* c, const float* a, const float* b, int64_t n, 
   if (!c || !a || !b) return mk::fail(MK_ERR_INVALID, "mk_vadd_f32: null pointer");
   cudaStream_t s = mk::as_stream(stream);
   const int64_t max_blocks = (int64_t)dev->sms * (2048 / kThreads);
+  const int64_t max_vblocks = (int64_t)dev->sms * kVecBlocksPerSM;
   if (mk::aligned16(a) && mk::aligned16(b) && mk::aligned16(c)) {
     const int64_t n4 = n / 4;
     if (n4 > 0) {
       int64_t blocks = mk::cdiv(n4, kThreads);
-      if (blocks > max_blocks) blocks = max_blocks;
+      if (blocks > max_vblocks) blocks = max_vblocks;
       // A 2^20-element vadd is over in ~3 us on the device; launched with
       // programmatic dependent launch so back-to-back launches (a stream of
       // small maps, or a CUDA graph of them) overlap their launch latency.
