@@ -8,7 +8,7 @@
 // Design (HBM-bound on the key stream; 4 or 8 bytes per key):
 //   * persistent grid (2 x 1024 threads per SM); every block privatises the
 //     whole histogram in shared memory as u32 counters; keys arrive as 16-byte
-//     vectors, two vectors in flight per thread;
+//     vectors, three vectors in flight per thread;
 //   * one shared atomic per key.  Warp aggregation with match.any measured 7x
 //     slower (instruction-issue bound) even on Zipf(1.1) keys, where one bin
 //     holds 16 % of the keys, and lane-spread replicas measured no faster:
@@ -33,7 +33,11 @@ namespace {
 
 constexpr int kThreads = 1024;
 constexpr int kBlocksPerSM = 2;
-constexpr int kUnroll = 2;
+// Key vectors in flight per thread: 3 x 16 B x 2048 threads = 96 KiB per SM
+// within the 32 registers that two 1024-thread blocks allow.  2^26 Zipf keys:
+// 2 -> 3 took a graph step from 45.6 to 43.6 us (0.84 -> 0.87 of HBM); 768-
+// thread blocks with 4 in flight measured the same, 5 or 6 in flight slower.
+constexpr int kUnroll = 3;
 
 template <typename K>
 struct KeyVec;
