@@ -88,13 +88,21 @@ class ClockSampler:
         self.proc = subprocess.Popen([exe, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                       "-i", str(self.dev), "-lms", "50"], stdout=self.fh,
                                      stderr=subprocess.DEVNULL)
-        time.sleep(0.15)
+        # nvidia-smi needs up to a second before its first sample: wait for it
+        # so that a short region (the GEMM's 20 steps take ~85 ms) is sampled
+        deadline = time.time() + 5.0
+        while time.time() < deadline and self.proc.poll() is None:
+            self.fh.flush()
+            if Path(self.path).read_text().count("\n") >= 1:
+                break
+            time.sleep(0.02)
+        self.skip = Path(self.path).read_text().count("\n")  # samples taken before the region
         return self
 
     def stop(self) -> dict | None:
         if self.proc is None:
             return None
-        time.sleep(0.1)
+        time.sleep(0.06)  # one more sampling period
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -107,6 +115,10 @@ class ClockSampler:
             if len(parts) >= 9:
                 rows.append(parts)
         os.unlink(self.path)
+        if len(rows) > self.skip:
+            rows = rows[self.skip:]
+        else:
+            rows = rows[-1:]  # region shorter than one period: the sample nearest its end
         if not rows:
             return None
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
