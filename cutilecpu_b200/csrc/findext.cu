@@ -14,6 +14,12 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kVec = 8;  // float4 loads in flight per thread
+// Minimum resident blocks per SM the register budget is fitted to: 4 leaves
+// 62 registers, so the eight vectors, the four candidate chains and their
+// 64-bit indices stay in registers.  At 6 (40 registers) the chains spilled
+// and findmax over 2^28 ran 0.191 ms (0.88 of HBM); at 4, 0.183 ms (0.92);
+// 5 measured 0.185 ms, six vectors at 6 per SM 0.194 ms.
+constexpr int kMinBlocks = 4;
 
 struct Cand {
   float v;
@@ -87,7 +93,7 @@ __device__ Cand block_best(Cand c, Cand* sm) {
 }
 
 template <bool MAX>
-__global__ void __launch_bounds__(kThreads, 6)
+__global__ void __launch_bounds__(kThreads, kMinBlocks)
 findext_kernel(const float* __restrict__ x, int64_t n, int head, float* __restrict__ pv, int64_t* __restrict__ pi,
                unsigned* __restrict__ ticket, double* __restrict__ val_out, int64_t* __restrict__ idx_out) {
   __shared__ Cand sm[kThreads / 32];
