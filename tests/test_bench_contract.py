@@ -36,3 +36,17 @@ def test_reference_arm_prints_the_same_config():
     assert line["metric"] == "vadd HBM GB/s" and line["unit"] == "GB/s" and line["higher_is_better"]
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+
+
+def test_clock_sampler_reports_a_sample_for_a_short_region(tmp_path, monkeypatch):
+    # a fake nvidia-smi that prints one CSV row every 50 ms after a slow start,
+    # like the real one; a region shorter than one period still gets a sample
+    fake = tmp_path / "nvidia-smi"
+    fake.write_text("#!/bin/sh\nsleep 0.3\nwhile true; do echo '0, 1965, 1965, 700.0, 0x0, Not Active, "
+                    "Not Active, Not Active, Active'; sleep 0.05; done\n")
+    fake.chmod(0o755)
+    monkeypatch.setenv("PATH", f"{tmp_path}:" + __import__("os").environ["PATH"])
+    c = bench.ClockSampler(0).start()
+    info = c.stop()
+    assert info is not None and info["samples"] >= 1
+    assert info["sm_mhz"] == 1965.0 and info["reasons"] == ["sw_power_cap"]
